@@ -1,0 +1,1110 @@
+// sm_100a kernels of the TextEngine decode path.
+//
+// Layouts (all row-major):
+//   weights   projection matrices are stored K-major, [out, in] — the transpose of the
+//             reference's Linear weight [in, out] (torch/Linear.java:20-27) — as float32 or bf16;
+//   residual  float32 [tokens, d];
+//   KV cache  per layer [rows][heads][slots][head_dim], float32 or bf16; a row's real tokens sit
+//             in slots 0..len-1 with slot == position.
+//
+// Every kernel computes in float32 (LayerNorm statistics and the sampler in float64, as the
+// reference does). Nothing here traps: invalid ids are rejected on the host before launch.
+
+#include "kernels.h"
+
+#include <cuda_bf16.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace bst {
+
+const char* kernel_class_name(int cls) {
+    static const char* names[kKernelClassCount] = {
+        "embed",       "layernorm",     "gemv",          "gemm",
+        "attn_decode", "attn_combine",  "attn_prefill",  "select_greedy",
+        "select_sample", "gather",      "head_last_token", "misc"};
+    return cls >= 0 && cls < kKernelClassCount ? names[cls] : "unknown";
+}
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kMaxChunk = 1024;
+constexpr size_t kSampleSmemLimit = 200 * 1024;
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float bf16_bits_to_f(uint32_t bits16) {
+    return __uint_as_float(bits16 << 16);
+}
+
+// One 16-byte load of weights/cache, unpacked to floats.
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<float> {
+    static constexpr int N = 4;
+    __device__ __forceinline__ static void load(const float* p, float* out) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+        out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+    }
+};
+template <>
+struct Vec16<__nv_bfloat16> {
+    static constexpr int N = 8;
+    __device__ __forceinline__ static void load(const __nv_bfloat16* p, float* out) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            out[2 * i] = bf16_bits_to_f(w[i] & 0xffffu);
+            out[2 * i + 1] = bf16_bits_to_f(w[i] >> 16);
+        }
+    }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// gelu_forward (nn_ops.rs:130-137): 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))), evaluated in
+// f32 in the reference's operation order without contraction.
+__device__ __forceinline__ float gelu_ref(float v) {
+    const float c = __fsqrt_rn(__fdiv_rn(2.0f, 3.14159274101257324f));
+    const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v);
+    const float inner = __fmul_rn(c, __fadd_rn(v, cube));
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <Epi E>
+__device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float v) {
+    if constexpr (E == Epi::kStore) {
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] = v;
+    } else if constexpr (E == Epi::kGelu) {
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] = gelu_ref(v);
+    } else if constexpr (E == Epi::kResidual) {
+        float* p = ea.out + static_cast<size_t>(m) * ea.ldo + n;
+        *p = __fadd_rn(*p, v);
+    } else if constexpr (E == Epi::kResidualGelu) {
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] =
+            gelu_ref(__fadd_rn(v, ea.res[static_cast<size_t>(m) * ea.ldr + n]));
+    } else if constexpr (E == Epi::kQkv) {
+        if (n < ea.d) {
+            ea.out[static_cast<size_t>(m) * ea.ldo + n] = v;
+        } else {
+            const int which = n / ea.d;
+            const int j = n - which * ea.d;
+            const int h = j / ea.head_dim;
+            const int e = j - h * ea.head_dim;
+            const size_t idx =
+                ((static_cast<size_t>(ea.rowmap[m]) * ea.heads + h) * ea.slots + ea.slot[m]) *
+                    ea.head_dim + e;
+            void* base = which == 1 ? ea.k_cache : ea.v_cache;
+            if (ea.kv_bf16) {
+                static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+            } else {
+                static_cast<float*>(base)[idx] = v;
+            }
+        }
+    } else if constexpr (E == Epi::kLogits) {
+        ea.out[static_cast<size_t>(ea.rowmap[m]) * ea.ldo + n] = v;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// GEMV for small M: each output column n is a dot product of W's row n (contiguous, K-major)
+// with up to MT activation rows. KS warps split one column's K range; 8 / KS columns per CTA.
+// Weight rows stream from HBM once with 16-byte coalesced loads; activations hit L1.
+// ---------------------------------------------------------------------------------------------
+template <typename WT, int MT, int KS, Epi E>
+__global__ __launch_bounds__(256) void k_gemv(const float* __restrict__ x, int ldx,
+                                              const WT* __restrict__ w,
+                                              const float* __restrict__ bias, int M, int N,
+                                              int K, EpiArgs ea) {
+    constexpr int VEC = Vec16<WT>::N;
+    constexpr int COLS = 8 / KS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int col = warp / KS, part = warp % KS;
+    const int n = blockIdx.x * COLS + col;
+    const int m0 = blockIdx.y * MT;
+    const int mcount = min(MT, M - m0);
+    float acc[MT];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) acc[i] = 0.0f;
+    if (n < N) {
+        const WT* wr = w + static_cast<size_t>(n) * K;
+        const float* xr = x + static_cast<size_t>(m0) * ldx;
+        if ((K % VEC) == 0 && (ldx % 4) == 0) {
+            const int nvec = K / VEC;
+            const int per = (nvec + KS - 1) / KS;
+            const int v0 = part * per, v1 = min(nvec, v0 + per);
+#pragma unroll 4
+            for (int v = v0 + lane; v < v1; v += 32) {
+                float wv[VEC];
+                Vec16<WT>::load(wr + static_cast<size_t>(v) * VEC, wv);
+                const int k = v * VEC;
+#pragma unroll
+                for (int i = 0; i < MT; ++i) {
+                    if (i < mcount) {
+                        const float* xp = xr + static_cast<size_t>(i) * ldx + k;
+#pragma unroll
+                        for (int c = 0; c < VEC; c += 4) {
+                            const float4 xv = *reinterpret_cast<const float4*>(xp + c);
+                            acc[i] = fmaf(wv[c], xv.x, acc[i]);
+                            acc[i] = fmaf(wv[c + 1], xv.y, acc[i]);
+                            acc[i] = fmaf(wv[c + 2], xv.z, acc[i]);
+                            acc[i] = fmaf(wv[c + 3], xv.w, acc[i]);
+                        }
+                    }
+                }
+            }
+        } else {
+            const int per = (K + KS - 1) / KS;
+            const int k0 = part * per, k1 = min(K, k0 + per);
+            for (int k = k0 + lane; k < k1; k += 32) {
+                const float wk = to_f(wr[k]);
+#pragma unroll
+                for (int i = 0; i < MT; ++i) {
+                    if (i < mcount) acc[i] = fmaf(wk, xr[static_cast<size_t>(i) * ldx + k], acc[i]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < MT; ++i) acc[i] = warp_sum(acc[i]);
+    __shared__ float red[8][MT];
+    if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < MT; ++i) red[warp][i] = acc[i];
+    }
+    __syncthreads();
+    if (part == 0 && lane < mcount && n < N) {
+        float s = 0.0f;
+#pragma unroll
+        for (int p = 0; p < KS; ++p) s += red[col * KS + p][lane];
+        const float v = bias ? __fadd_rn(s, bias[n]) : s;
+        epi_apply<E>(ea, m0 + lane, n, v);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Tiled FFMA GEMM for larger M: 128x128 tile, k-step 16, 8x8 outputs per thread, double-buffered
+// shared tiles. A is float32 [M, K]; B is [N, K] (float32 or bf16, converted on load).
+// Requires K % 16 == 0.
+// ---------------------------------------------------------------------------------------------
+template <typename WT, Epi E>
+__global__ __launch_bounds__(256) void k_gemm(const float* __restrict__ a, int lda,
+                                              const WT* __restrict__ b,
+                                              const float* __restrict__ bias, int M, int N,
+                                              int K, EpiArgs ea) {
+    constexpr int BM = 128, BN = 128, BK = 16, PAD = 4;
+    __shared__ __align__(16) float As[2][BK][BM + PAD];
+    __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int tx = tid & 15, ty = tid >> 4;
+
+    float4 ra[2];
+    float rb[8];
+    auto load_tile = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int idx = tid + 256 * i;
+            const int row = idx >> 2, kq = idx & 3;
+            const int m = m0 + row;
+            ra[i] = m < M ? *reinterpret_cast<const float4*>(a + static_cast<size_t>(m) * lda +
+                                                             k0 + kq * 4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if constexpr (sizeof(WT) == 4) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int idx = tid + 256 * i;
+                const int row = idx >> 2, kq = idx & 3;
+                const int n = n0 + row;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (n < N) {
+                    v = __ldg(reinterpret_cast<const float4*>(
+                        reinterpret_cast<const float*>(b) + static_cast<size_t>(n) * K + k0 +
+                        kq * 4));
+                }
+                rb[4 * i] = v.x; rb[4 * i + 1] = v.y; rb[4 * i + 2] = v.z; rb[4 * i + 3] = v.w;
+            }
+        } else {
+            const int row = tid >> 1, kh = tid & 1;
+            const int n = n0 + row;
+            if (n < N) {
+                Vec16<WT>::load(b + static_cast<size_t>(n) * K + k0 + kh * 8, rb);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) rb[c] = 0.0f;
+            }
+        }
+    };
+    auto store_tile = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int idx = tid + 256 * i;
+            const int row = idx >> 2, kq = idx & 3;
+            As[buf][kq * 4 + 0][row] = ra[i].x;
+            As[buf][kq * 4 + 1][row] = ra[i].y;
+            As[buf][kq * 4 + 2][row] = ra[i].z;
+            As[buf][kq * 4 + 3][row] = ra[i].w;
+        }
+        if constexpr (sizeof(WT) == 4) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int idx = tid + 256 * i;
+                const int row = idx >> 2, kq = idx & 3;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) Bs[buf][kq * 4 + c][row] = rb[4 * i + c];
+            }
+        } else {
+            const int row = tid >> 1, kh = tid & 1;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) Bs[buf][kh * 8 + c][row] = rb[c];
+        }
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+    load_tile(0);
+    store_tile(0);
+    __syncthreads();
+    for (int k0 = 0; k0 < K; k0 += BK) {
+        const int buf = (k0 / BK) & 1;
+        const bool more = k0 + BK < K;
+        if (more) load_tile(k0 + BK);
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (more) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+            if (n >= N) continue;
+            const float v = bias ? __fadd_rn(acc[i][j], bias[n]) : acc[i][j];
+            epi_apply<E>(ea, m, n, v);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Embedding gathers.
+// ---------------------------------------------------------------------------------------------
+template <typename WT>
+__global__ void k_embed_tokens(const WT* __restrict__ tok, const WT* __restrict__ pos,
+                               const int* __restrict__ ids, const int* __restrict__ positions,
+                               float* __restrict__ x, int d) {
+    const int t = blockIdx.x;
+    const size_t id = static_cast<size_t>(ids[t]);
+    const size_t p = static_cast<size_t>(positions[t]);
+    for (int e = threadIdx.x; e < d; e += blockDim.x) {
+        x[static_cast<size_t>(t) * d + e] = __fadd_rn(to_f(tok[id * d + e]), to_f(pos[p * d + e]));
+    }
+}
+
+template <typename WT>
+__global__ void k_embed_decode(const WT* __restrict__ tok, const WT* __restrict__ pos,
+                               const int* __restrict__ rowmap, const int* __restrict__ next,
+                               int* __restrict__ len, int* __restrict__ slot,
+                               float* __restrict__ x, int d) {
+    const int i = blockIdx.x;
+    const int row = rowmap[i];
+    __shared__ int s_slot;
+    if (threadIdx.x == 0) s_slot = len[row];
+    __syncthreads();
+    const int sl = s_slot;
+    const size_t id = static_cast<size_t>(next[row]);
+    for (int e = threadIdx.x; e < d; e += blockDim.x) {
+        x[static_cast<size_t>(i) * d + e] =
+            __fadd_rn(to_f(tok[id * d + e]), to_f(pos[static_cast<size_t>(sl) * d + e]));
+    }
+    if (threadIdx.x == 0) {
+        slot[i] = sl;
+        len[row] = sl + 1;
+    }
+}
+
+template <typename WT>
+__global__ void k_window_embed(const int* __restrict__ window, int W, const WT* __restrict__ emb,
+                               int d, float* __restrict__ x) {
+    const int r = blockIdx.x;
+    for (int idx = threadIdx.x; idx < W * d; idx += blockDim.x) {
+        const int t = idx / d, e = idx - t * d;
+        const size_t id = static_cast<size_t>(window[static_cast<size_t>(r) * W + t]);
+        x[static_cast<size_t>(r) * W * d + idx] = to_f(emb[id * d + e]);
+    }
+}
+
+__global__ void k_last_token(const int* __restrict__ window, int W, const float* __restrict__ w,
+                             const float* __restrict__ bias, int V, float* __restrict__ logits) {
+    const int r = blockIdx.x;
+    const int token = window[static_cast<size_t>(r) * W + W - 1];
+    const int t = ((token % V) + V) % V;  // Math.floorMod
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        logits[static_cast<size_t>(r) * V + v] =
+            __fadd_rn(w[static_cast<size_t>(t) * V + v], bias[v]);
+    }
+}
+
+__global__ void k_prefill_tokens(const int* __restrict__ window, int W,
+                                 const int* __restrict__ seg_row, const int* __restrict__ seg_npad,
+                                 const int* __restrict__ seg_start, const int* __restrict__ seg_len,
+                                 int pad_id, int* __restrict__ ids, int* __restrict__ positions,
+                                 int* __restrict__ tok_row, int* __restrict__ len) {
+    const int j = blockIdx.x;
+    const int row = seg_row[j], npad = seg_npad[j], start = seg_start[j], n = seg_len[j];
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        ids[start + t] = npad >= W ? pad_id : window[static_cast<size_t>(row) * W + npad + t];
+        positions[start + t] = t;
+        tok_row[start + t] = row;
+    }
+    if (threadIdx.x == 0) len[row] = n;
+}
+
+__global__ void k_gather_last(const float* __restrict__ x, const int* __restrict__ seg_start,
+                              const int* __restrict__ seg_len, int d, float* __restrict__ last) {
+    const int j = blockIdx.x;
+    const size_t src = static_cast<size_t>(seg_start[j] + seg_len[j] - 1) * d;
+    for (int e = threadIdx.x; e < d; e += blockDim.x) last[static_cast<size_t>(j) * d + e] = x[src + e];
+}
+
+// ---------------------------------------------------------------------------------------------
+// LayerNorm (nn_ops.rs:168-199): one warp per row; mean and population variance in f64, the
+// normalised value rounded to f32, then f32 n * gamma + beta.
+// ---------------------------------------------------------------------------------------------
+__global__ __launch_bounds__(256) void k_layernorm(const float* __restrict__ x, int ldx,
+                                                   const float* __restrict__ gamma,
+                                                   const float* __restrict__ beta,
+                                                   float* __restrict__ y, int ldy, int rows, int d,
+                                                   float eps) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + warp;
+    if (row >= rows) return;
+    const float* xr = x + static_cast<size_t>(row) * ldx;
+    float* yr = y + static_cast<size_t>(row) * ldy;
+    double s = 0.0;
+    for (int i = lane; i < d; i += 32) s = __dadd_rn(s, static_cast<double>(xr[i]));
+    const double mean = __ddiv_rn(warp_sum_d(s), static_cast<double>(d));
+    double v = 0.0;
+    for (int i = lane; i < d; i += 32) {
+        const double delta = __dadd_rn(static_cast<double>(xr[i]), -mean);
+        v = __dadd_rn(v, __dmul_rn(delta, delta));
+    }
+    const double variance = __ddiv_rn(warp_sum_d(v), static_cast<double>(d));
+    const double inverse = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(eps))));
+    for (int i = lane; i < d; i += 32) {
+        const float normalized =
+            static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(xr[i]), -mean), inverse));
+        yr[i] = __fadd_rn(__fmul_rn(normalized, gamma[i]), beta[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Decode attention, split over the cached keys. One CTA per (row, head, split); writes the
+// split's running max, sum of exponentials and unnormalised output. Scores follow
+// MultiheadAttention.forward (MultiheadAttention.java:57-82): dot(q, k) then * scale (f32).
+// ---------------------------------------------------------------------------------------------
+template <typename KT, int HD>
+__global__ __launch_bounds__(128) void k_attn_decode(
+    const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
+    const int* __restrict__ rowmap, const int* __restrict__ len, int heads, int slots,
+    float scale, int splits, int chunk, float* __restrict__ part) {
+    constexpr int EPV = Vec16<KT>::N;
+    constexpr int LPK = HD / EPV;  // lanes per key
+    constexpr int KPW = 32 / LPK;  // keys per warp step
+    constexpr int DPL = HD / 32;   // output dims per lane
+    const int i = blockIdx.x / heads, h = blockIdx.x % heads, sp = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row = rowmap[i];
+    const int T = len[row];
+    const int start = sp * chunk, end = min(T, start + chunk);
+    const int d = heads * HD;
+    __shared__ float qs[HD];
+    __shared__ float sc[kMaxChunk];
+    __shared__ float red[4 * HD];
+    __shared__ float stat[8];
+    float* out = part + (static_cast<size_t>(i * heads + h) * splits + sp) * (HD + 2);
+    if (start >= end) {
+        for (int e = tid; e < HD; e += 128) out[e] = 0.0f;
+        if (tid == 0) {
+            out[HD] = -INFINITY;
+            out[HD + 1] = 0.0f;
+        }
+        return;
+    }
+    for (int e = tid; e < HD; e += 128) qs[e] = q[static_cast<size_t>(i) * d + h * HD + e];
+    __syncthreads();
+    const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
+    const int n = end - start;
+    const int sub = lane % LPK, kk = lane / LPK;
+    for (int j0 = warp * KPW; j0 < n; j0 += 4 * KPW) {
+        const int j = j0 + kk;
+        float dot = 0.0f;
+        if (j < n) {
+            float kv[EPV];
+            Vec16<KT>::load(kc + (base + j) * HD + sub * EPV, kv);
+#pragma unroll
+            for (int c = 0; c < EPV; ++c) dot = fmaf(kv[c], qs[sub * EPV + c], dot);
+        }
+#pragma unroll
+        for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(kFull, dot, o);
+        if (sub == 0 && j < n) sc[j] = __fmul_rn(dot, scale);
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = tid; j < n; j += 128) mx = fmaxf(mx, sc[j]);
+    mx = warp_max(mx);
+    if (lane == 0) stat[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(stat[0], stat[1]), fmaxf(stat[2], stat[3]));
+    float sum = 0.0f;
+    for (int j = tid; j < n; j += 128) {
+        const float p = expf(sc[j] - mx);
+        sc[j] = p;
+        sum += p;
+    }
+    sum = warp_sum(sum);
+    __syncthreads();
+    if (lane == 0) stat[4 + warp] = sum;
+    __syncthreads();
+    sum = stat[4] + stat[5] + stat[6] + stat[7];
+    float o[DPL];
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) o[c] = 0.0f;
+    for (int j = warp; j < n; j += 4) {
+        const float p = sc[j];
+        const KT* vr = vc + (base + j) * HD + lane * DPL;
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) o[c] = fmaf(p, to_f(vr[c]), o[c]);
+    }
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) red[warp * HD + lane * DPL + c] = o[c];
+    __syncthreads();
+    for (int e = tid; e < HD; e += 128) out[e] = red[e] + red[HD + e] + red[2 * HD + e] + red[3 * HD + e];
+    if (tid == 0) {
+        out[HD] = mx;
+        out[HD + 1] = sum;
+    }
+}
+
+template <int HD>
+__global__ void k_attn_combine(const float* __restrict__ part, int splits, int heads,
+                               float* __restrict__ out) {
+    const int ih = blockIdx.x;
+    const int i = ih / heads, h = ih % heads;
+    const float* p = part + static_cast<size_t>(ih) * splits * (HD + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (HD + 2) + HD]);
+    for (int e = threadIdx.x; e < HD; e += blockDim.x) {
+        float L = 0.0f, O = 0.0f;
+        for (int s = 0; s < splits; ++s) {
+            const float ms = p[s * (HD + 2) + HD];
+            if (ms == -INFINITY) continue;
+            const float wgt = expf(ms - M);
+            L = fmaf(p[s * (HD + 2) + HD + 1], wgt, L);
+            O = fmaf(p[s * (HD + 2) + e], wgt, O);
+        }
+        out[static_cast<size_t>(i) * heads * HD + h * HD + e] = O / L;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Causal prefill attention over one row's freshly written cache slots. CTA = (segment, head,
+// tile of 4*QPW queries); keys stream through shared memory 32 at a time with an online softmax.
+// ---------------------------------------------------------------------------------------------
+template <typename KT, int HD, int QPW>
+__global__ __launch_bounds__(128) void k_attn_prefill(
+    const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
+    const int* __restrict__ seg_row, const int* __restrict__ seg_start,
+    const int* __restrict__ seg_len, int heads, int slots, float scale, float* __restrict__ out) {
+    constexpr int QT = 4 * QPW;
+    constexpr int DPL = HD / 32;
+    const int j = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * QT;
+    const int n = seg_len[j];
+    if (t0 >= n) return;
+    const int row = seg_row[j], start = seg_start[j], d = heads * HD;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float Qs[QT][HD];
+    __shared__ float Kt[HD][33];
+    __shared__ float Vs[32][HD];
+    for (int idx = tid; idx < QT * HD; idx += 128) {
+        const int r = idx / HD, e = idx - r * HD;
+        const int t = t0 + r;
+        Qs[r][e] = t < n ? q[static_cast<size_t>(start + t) * d + h * HD + e] : 0.0f;
+    }
+    float m[QPW], l[QPW], o[QPW][DPL];
+#pragma unroll
+    for (int r = 0; r < QPW; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) o[r][c] = 0.0f;
+    }
+    const size_t base = (static_cast<size_t>(row) * heads + h) * slots;
+    const int kend = min(n, t0 + QT);
+    for (int kb = 0; kb < kend; kb += 32) {
+        __syncthreads();
+        for (int idx = tid; idx < 32 * HD; idx += 128) {
+            const int r = idx / HD, e = idx - r * HD;
+            const int key = kb + r;
+            float kv = 0.0f, vv = 0.0f;
+            if (key < n) {
+                kv = to_f(kc[(base + key) * HD + e]);
+                vv = to_f(vc[(base + key) * HD + e]);
+            }
+            Kt[e][r] = kv;
+            Vs[r][e] = vv;
+        }
+        __syncthreads();
+        const int key = kb + lane;
+#pragma unroll
+        for (int r = 0; r < QPW; ++r) {
+            const int qi = warp * QPW + r;
+            const int t = t0 + qi;
+            float s = -INFINITY;
+            if (t < n && key <= t) {
+                float dot = 0.0f;
+#pragma unroll 16
+                for (int e = 0; e < HD; ++e) dot = fmaf(Qs[qi][e], Kt[e][lane], dot);
+                s = __fmul_rn(dot, scale);
+            }
+            const float mnew = fmaxf(m[r], warp_max(s));
+            if (mnew == -INFINITY) continue;
+            const float p = s == -INFINITY ? 0.0f : expf(s - mnew);
+            const float corr = m[r] == -INFINITY ? 0.0f : expf(m[r] - mnew);
+            l[r] = l[r] * corr + warp_sum(p);
+#pragma unroll
+            for (int c = 0; c < DPL; ++c) o[r][c] *= corr;
+            for (int kk = 0; kk < 32; ++kk) {
+                const float pk = __shfl_sync(kFull, p, kk);
+#pragma unroll
+                for (int c = 0; c < DPL; ++c) o[r][c] = fmaf(pk, Vs[kk][lane * DPL + c], o[r][c]);
+            }
+            m[r] = mnew;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < QPW; ++r) {
+        const int t = t0 + warp * QPW + r;
+        if (t >= n) continue;
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) {
+            out[static_cast<size_t>(start + t) * d + h * HD + lane * DPL + c] = o[r][c] / l[r];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Token selection and step bookkeeping.
+// ---------------------------------------------------------------------------------------------
+// Writes the chosen token, shifts the row's window (TextEngine.push, TextEngine.java:387-390) and
+// advances the step counter once the last row of the step is done.
+__device__ void finish_row(int r, int token, int g, int rows, int W, int steps, int* step,
+                           int* done, int* tokens, int* next, int* window) {
+    int* win = window + static_cast<size_t>(r) * W;
+    constexpr int kPerThread = 8;
+    int carry[kPerThread];
+#pragma unroll
+    for (int c = 0; c < kPerThread; ++c) {
+        const int t = threadIdx.x + c * blockDim.x;
+        carry[c] = t + 1 < W ? win[t + 1] : token;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < kPerThread; ++c) {
+        const int t = threadIdx.x + c * blockDim.x;
+        if (t < W) win[t] = carry[c];
+    }
+    if (threadIdx.x == 0) {
+        tokens[static_cast<size_t>(r) * steps + g] = token;
+        next[r] = token;
+        __threadfence();
+        const int prev = atomicAdd(done, 1);
+        if (prev == rows - 1) {
+            *done = 0;
+            *step = g + 1;
+            __threadfence();
+        }
+    }
+}
+
+// TextEngine.argmax (TextEngine.java:392-400): strict '>' so the first maximum wins.
+__global__ __launch_bounds__(256) void k_select_greedy(const float* __restrict__ logits, int V,
+                                                       int W, int steps, int rows, int* step,
+                                                       int* done, int* tokens, int* next,
+                                                       int* window) {
+    const int r = blockIdx.x;
+    const float* lr = logits + static_cast<size_t>(r) * V;
+    __shared__ int s_step;
+    __shared__ float s_val[8];
+    __shared__ int s_idx[8];
+    if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile int*>(step);
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float x = lr[v];
+        if (isnan(x)) continue;
+        if (x > best || (x == best && v < bi)) {
+            best = x;
+            bi = v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, best, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        s_val[warp] = best;
+        s_idx[warp] = bi;
+    }
+    __syncthreads();
+    __shared__ int s_token;
+    if (threadIdx.x == 0) {
+        for (int w2 = 1; w2 < static_cast<int>(blockDim.x >> 5); ++w2) {
+            if (s_val[w2] > best || (s_val[w2] == best && s_idx[w2] < bi)) {
+                best = s_val[w2];
+                bi = s_idx[w2];
+            }
+        }
+        // A NaN first score is never replaced (no value compares greater than it).
+        s_token = (isnan(lr[0]) || bi == 0x7fffffff) ? 0 : bi;
+    }
+    __syncthreads();
+    finish_row(r, s_token, s_step, rows, W, steps, step, done, tokens, next, window);
+}
+
+// java.util.Random step and nextDouble (JDK specification).
+__device__ __forceinline__ int rng_next(uint64_t& s, int bits) {
+    s = (s * 0x5DEECE66DULL + 0xBULL) & ((1ULL << 48) - 1);
+    return static_cast<int>(static_cast<int64_t>(s) >> (48 - bits));
+}
+__device__ __forceinline__ double rng_next_double(uint64_t& s) {
+    const int64_t hi = rng_next(s, 26);
+    const int64_t lo = rng_next(s, 27);
+    return static_cast<double>((hi << 27) + lo) * 0x1.0p-53;
+}
+
+// Sort key: ascending key order == descending Double.compare order, ties by ascending index
+// (the stable List.sort of TextEngine.java:408). -0.0 sorts after +0.0 and NaN first, as
+// Double.compare orders them.
+__device__ __forceinline__ uint64_t sort_key(float value, int index) {
+    uint32_t f = __float_as_uint(value);
+    if (isnan(value)) f = 0x7fc00000u;
+    const uint32_t ascending = (f & 0x80000000u) ? ~f : (f | 0x80000000u);
+    return (static_cast<uint64_t>(~ascending) << 32) | static_cast<uint32_t>(index);
+}
+
+// TextEngine.draw (TextEngine.java:403-427): stable descending sort, w_i = exp((s_i - max) / T)
+// in double over the first topK, total summed in sorted order, target = nextDouble() * total,
+// first i with target <= running sum (else topK - 1). The sums run sequentially in one thread so
+// they round exactly as the reference's loop does.
+__global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict__ logits, int V,
+                                                        int P, int W, int steps, int rows,
+                                                        double temperature, int top_k,
+                                                        uint64_t* rng, int* step, int* done,
+                                                        int* tokens, int* next, int* window) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint64_t* keys = reinterpret_cast<uint64_t*>(smem);
+    int* order = reinterpret_cast<int*>(keys + P);
+    const int r = blockIdx.x;
+    const float* lr = logits + static_cast<size_t>(r) * V;
+    __shared__ int s_step, s_token;
+    if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile int*>(step);
+    for (int v = threadIdx.x; v < P; v += blockDim.x) keys[v] = v < V ? sort_key(lr[v], v) : ~0ULL;
+    __syncthreads();
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t a = keys[i], b = keys[ixj];
+                    if ((a > b) == ((i & k) == 0)) {
+                        keys[i] = b;
+                        keys[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = threadIdx.x; i < top_k; i += blockDim.x) order[i] = static_cast<int>(keys[i] & 0xffffffffu);
+    __syncthreads();
+    double* weights = reinterpret_cast<double*>(keys);  // reuse: keys are no longer needed
+    const double maximum = static_cast<double>(lr[order[0]]);
+    for (int i = threadIdx.x; i < top_k; i += blockDim.x) {
+        weights[i] = exp(__ddiv_rn(__dadd_rn(static_cast<double>(lr[order[i]]), -maximum), temperature));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double total = 0.0;
+        for (int i = 0; i < top_k; ++i) total = __dadd_rn(total, weights[i]);
+        uint64_t state = rng[r];
+        const double target = __dmul_rn(rng_next_double(state), total);
+        rng[r] = state;
+        double running = 0.0;
+        int chosen = order[top_k - 1];
+        for (int i = 0; i < top_k; ++i) {
+            running = __dadd_rn(running, weights[i]);
+            if (target <= running) {
+                chosen = order[i];
+                break;
+            }
+        }
+        s_token = chosen;
+    }
+    __syncthreads();
+    finish_row(r, s_token, s_step, rows, W, steps, step, done, tokens, next, window);
+}
+
+__global__ void k_stash_logits(const float* __restrict__ logits, int V, int steps,
+                               const int* __restrict__ step, float* __restrict__ history) {
+    const int r = blockIdx.y;
+    const int g = *step;
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v < V) {
+        history[(static_cast<size_t>(r) * steps + g) * V + v] = logits[static_cast<size_t>(r) * V + v];
+    }
+}
+
+__global__ void k_fill_int(int* p, int value, int count) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) p[i] = value;
+}
+__global__ void k_iota(int* p, int count) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) p[i] = i;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Dispatch helpers.
+// ---------------------------------------------------------------------------------------------
+int pick_ks(int columns, int row_groups, int nvec) {
+    // Enough CTAs to cover 2 waves of 148 SMs, but every warp keeps at least one full pass.
+    int ks = 1;
+    while (ks < 8) {
+        const long ctas = static_cast<long>((columns + (8 / ks) - 1) / (8 / ks)) * row_groups;
+        if (ctas >= 296 || nvec < 64 * ks) break;
+        ks *= 2;
+    }
+    return ks;
+}
+
+template <typename WT, int MT, Epi E>
+cudaError_t gemv_ks(cudaStream_t s, const float* x, int ldx, const void* w, const float* bias,
+                    int M, int N, int K, const EpiArgs& ea) {
+    const int row_groups = (M + MT - 1) / MT;
+    const int ks = pick_ks(N, row_groups, K / Vec16<WT>::N);
+    const WT* wt = static_cast<const WT*>(w);
+    const dim3 block(256);
+    switch (ks) {
+        case 1: k_gemv<WT, MT, 1, E><<<dim3((N + 7) / 8, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
+        case 2: k_gemv<WT, MT, 2, E><<<dim3((N + 3) / 4, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
+        case 4: k_gemv<WT, MT, 4, E><<<dim3((N + 1) / 2, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
+        default: k_gemv<WT, MT, 8, E><<<dim3(N, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
+    }
+    return cudaGetLastError();
+}
+
+template <typename WT, Epi E>
+cudaError_t linear_typed(cudaStream_t s, const float* x, int ldx, const void* w,
+                         const float* bias, int M, int N, int K, const EpiArgs& ea) {
+    if (linear_uses_gemv(M, N, K)) {
+        if (M == 1) return gemv_ks<WT, 1, E>(s, x, ldx, w, bias, M, N, K, ea);
+        return gemv_ks<WT, 8, E>(s, x, ldx, w, bias, M, N, K, ea);
+    }
+    const dim3 grid((N + 127) / 128, (M + 127) / 128);
+    k_gemm<WT, E><<<grid, 256, 0, s>>>(x, ldx, static_cast<const WT*>(w), bias, M, N, K, ea);
+    return cudaGetLastError();
+}
+
+template <typename WT>
+cudaError_t linear_epi(cudaStream_t s, const float* x, int ldx, const void* w, const float* bias,
+                       int M, int N, int K, Epi epi, const EpiArgs& ea) {
+    switch (epi) {
+        case Epi::kStore: return linear_typed<WT, Epi::kStore>(s, x, ldx, w, bias, M, N, K, ea);
+        case Epi::kGelu: return linear_typed<WT, Epi::kGelu>(s, x, ldx, w, bias, M, N, K, ea);
+        case Epi::kResidual: return linear_typed<WT, Epi::kResidual>(s, x, ldx, w, bias, M, N, K, ea);
+        case Epi::kResidualGelu: return linear_typed<WT, Epi::kResidualGelu>(s, x, ldx, w, bias, M, N, K, ea);
+        case Epi::kQkv: return linear_typed<WT, Epi::kQkv>(s, x, ldx, w, bias, M, N, K, ea);
+        case Epi::kLogits: return linear_typed<WT, Epi::kLogits>(s, x, ldx, w, bias, M, N, K, ea);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+bool linear_uses_gemv(int M, int N, int K) {
+    (void)N;
+    return M <= 8 || (K % 16) != 0;
+}
+
+cudaError_t launch_linear(cudaStream_t s, const float* x, int ldx, const void* w, int w_bf16,
+                          const float* bias, int M, int N, int K, Epi epi, const EpiArgs& ea) {
+    if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+    return w_bf16 ? linear_epi<__nv_bfloat16>(s, x, ldx, w, bias, M, N, K, epi, ea)
+                  : linear_epi<float>(s, x, ldx, w, bias, M, N, K, epi, ea);
+}
+
+cudaError_t launch_embed_tokens(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
+                                const int* ids, const int* positions, float* x, int count,
+                                int d) {
+    if (count <= 0) return cudaSuccess;
+    const int threads = d >= 256 ? 256 : 128;
+    if (w_bf16) {
+        k_embed_tokens<__nv_bfloat16><<<count, threads, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(tok), static_cast<const __nv_bfloat16*>(pos), ids,
+            positions, x, d);
+    } else {
+        k_embed_tokens<float><<<count, threads, 0, s>>>(static_cast<const float*>(tok),
+                                                        static_cast<const float*>(pos), ids,
+                                                        positions, x, d);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
+                                const int* rowmap, const int* next, int* len, int* slot, float* x,
+                                int R, int d) {
+    if (R <= 0) return cudaSuccess;
+    const int threads = d >= 256 ? 256 : 128;
+    if (w_bf16) {
+        k_embed_decode<__nv_bfloat16><<<R, threads, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(tok), static_cast<const __nv_bfloat16*>(pos),
+            rowmap, next, len, slot, x, d);
+    } else {
+        k_embed_decode<float><<<R, threads, 0, s>>>(static_cast<const float*>(tok),
+                                                    static_cast<const float*>(pos), rowmap, next,
+                                                    len, slot, x, d);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const float* gamma,
+                             const float* beta, float* y, int ldy, int rows, int d, float eps) {
+    if (rows <= 0) return cudaSuccess;
+    k_layernorm<<<(rows + 7) / 8, 256, 0, s>>>(x, ldx, gamma, beta, y, ldy, rows, d, eps);
+    return cudaGetLastError();
+}
+
+namespace {
+template <typename KT, int HD>
+cudaError_t attn_decode_typed(cudaStream_t s, const float* q, const void* kc, const void* vc,
+                              const int* rowmap, const int* len, int R, int heads, int slots,
+                              float scale, int splits, int chunk, float* part) {
+    k_attn_decode<KT, HD><<<dim3(R * heads, splits), 128, 0, s>>>(
+        q, static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len, heads, slots,
+        scale, splits, chunk, part);
+    return cudaGetLastError();
+}
+
+template <typename KT, int HD>
+cudaError_t attn_prefill_typed(cudaStream_t s, const float* q, const void* kc, const void* vc,
+                               const int* seg_row, const int* seg_start, const int* seg_len,
+                               int segments, int max_len, int heads, int slots, float scale,
+                               float* out) {
+    constexpr int QPW = HD > 64 ? 4 : 8;
+    const dim3 grid(segments, heads, (max_len + 4 * QPW - 1) / (4 * QPW));
+    k_attn_prefill<KT, HD, QPW><<<grid, 128, 0, s>>>(
+        q, static_cast<const KT*>(kc), static_cast<const KT*>(vc), seg_row, seg_start, seg_len,
+        heads, slots, scale, out);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
+                               const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
+                               int R, int heads, int head_dim, int slots, float scale, int splits,
+                               int chunk, float* part) {
+    if (R <= 0) return cudaSuccess;
+    if (chunk > kMaxChunk) return cudaErrorInvalidValue;
+#define BST_ATTN_DEC(KT, HD)                                                                    \
+    return attn_decode_typed<KT, HD>(s, q, k_cache, v_cache, rowmap, len, R, heads, slots,      \
+                                     scale, splits, chunk, part)
+    if (kv_bf16) {
+        switch (head_dim) {
+            case 32: BST_ATTN_DEC(__nv_bfloat16, 32);
+            case 64: BST_ATTN_DEC(__nv_bfloat16, 64);
+            case 128: BST_ATTN_DEC(__nv_bfloat16, 128);
+        }
+    } else {
+        switch (head_dim) {
+            case 32: BST_ATTN_DEC(float, 32);
+            case 64: BST_ATTN_DEC(float, 64);
+            case 128: BST_ATTN_DEC(float, 128);
+        }
+    }
+#undef BST_ATTN_DEC
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_attn_combine(cudaStream_t s, const float* part, int R, int heads, int head_dim,
+                                int splits, float* out) {
+    if (R <= 0) return cudaSuccess;
+    switch (head_dim) {
+        case 32: k_attn_combine<32><<<R * heads, 32, 0, s>>>(part, splits, heads, out); break;
+        case 64: k_attn_combine<64><<<R * heads, 64, 0, s>>>(part, splits, heads, out); break;
+        case 128: k_attn_combine<128><<<R * heads, 128, 0, s>>>(part, splits, heads, out); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,
+                                const void* v_cache, int kv_bf16, const int* seg_row,
+                                const int* seg_start, const int* seg_len, int segments,
+                                int max_len, int heads, int head_dim, int slots, float scale,
+                                float* out) {
+    if (segments <= 0) return cudaSuccess;
+#define BST_ATTN_PRE(KT, HD)                                                                    \
+    return attn_prefill_typed<KT, HD>(s, q, k_cache, v_cache, seg_row, seg_start, seg_len,      \
+                                      segments, max_len, heads, slots, scale, out)
+    if (kv_bf16) {
+        switch (head_dim) {
+            case 32: BST_ATTN_PRE(__nv_bfloat16, 32);
+            case 64: BST_ATTN_PRE(__nv_bfloat16, 64);
+            case 128: BST_ATTN_PRE(__nv_bfloat16, 128);
+        }
+    } else {
+        switch (head_dim) {
+            case 32: BST_ATTN_PRE(float, 32);
+            case 64: BST_ATTN_PRE(float, 64);
+            case 128: BST_ATTN_PRE(float, 128);
+        }
+    }
+#undef BST_ATTN_PRE
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_prefill_tokens(cudaStream_t s, const int* window, int W, const int* seg_row,
+                                  const int* seg_npad, const int* seg_start, const int* seg_len,
+                                  int segments, int pad_id, int* ids, int* positions, int* tok_row,
+                                  int* len) {
+    if (segments <= 0) return cudaSuccess;
+    k_prefill_tokens<<<segments, 256, 0, s>>>(window, W, seg_row, seg_npad, seg_start, seg_len,
+                                              pad_id, ids, positions, tok_row, len);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_last(cudaStream_t s, const float* x, const int* seg_start,
+                               const int* seg_len, int segments, int d, float* last) {
+    if (segments <= 0) return cudaSuccess;
+    k_gather_last<<<segments, 128, 0, s>>>(x, seg_start, seg_len, d, last);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_window_embed(cudaStream_t s, const int* window, int W, const void* emb,
+                                int w_bf16, int rows, int d, float* x) {
+    if (rows <= 0) return cudaSuccess;
+    if (w_bf16) {
+        k_window_embed<__nv_bfloat16><<<rows, 256, 0, s>>>(
+            window, W, static_cast<const __nv_bfloat16*>(emb), d, x);
+    } else {
+        k_window_embed<float><<<rows, 256, 0, s>>>(window, W, static_cast<const float*>(emb), d,
+                                                   x);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_last_token(cudaStream_t s, const int* window, int W, const float* weight,
+                              const float* bias, int rows, int V, float* logits) {
+    if (rows <= 0) return cudaSuccess;
+    k_last_token<<<rows, 128, 0, s>>>(window, W, weight, bias, V, logits);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, int V, int W,
+                                 int steps, int* step, int* done, int* tokens, int* next,
+                                 int* window) {
+    if (rows <= 0) return cudaSuccess;
+    if (W > 8 * 256) return cudaErrorInvalidValue;
+    k_select_greedy<<<rows, 256, 0, s>>>(logits, V, W, steps, rows, step, done, tokens, next,
+                                         window);
+    return cudaGetLastError();
+}
+
+size_t select_sample_smem(int V) {
+    int P = 1;
+    while (P < V) P <<= 1;
+    return static_cast<size_t>(P) * (sizeof(uint64_t) + sizeof(int));
+}
+
+cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, int V, int W,
+                                 int steps, float temperature, int top_k, uint64_t* rng,
+                                 int* step, int* done, int* tokens, int* next, int* window) {
+    if (rows <= 0) return cudaSuccess;
+    if (W > 8 * 1024) return cudaErrorInvalidValue;
+    int P = 1;
+    while (P < V) P <<= 1;
+    const size_t smem = select_sample_smem(V);
+    if (smem > kSampleSmemLimit) return cudaErrorInvalidValue;
+    k_select_sample<<<rows, 1024, smem, s>>>(logits, V, P, W, steps, rows,
+                                             static_cast<double>(temperature), top_k, rng, step,
+                                             done, tokens, next, window);
+    return cudaGetLastError();
+}
+
+cudaError_t configure_device_kernels() {
+    return cudaFuncSetAttribute(k_select_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kSampleSmemLimit));
+}
+
+cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,
+                                const int* step, float* history) {
+    if (rows <= 0) return cudaSuccess;
+    k_stash_logits<<<dim3((V + 255) / 256, rows), 256, 0, s>>>(logits, V, steps, step, history);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill_int(cudaStream_t s, int* p, int value, int count) {
+    if (count <= 0) return cudaSuccess;
+    k_fill_int<<<(count + 255) / 256, 256, 0, s>>>(p, value, count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_iota(cudaStream_t s, int* p, int count) {
+    if (count <= 0) return cudaSuccess;
+    k_iota<<<(count + 255) / 256, 256, 0, s>>>(p, count);
+    return cudaGetLastError();
+}
+
+}  // namespace bst

@@ -1,0 +1,128 @@
+// Host-side launchers for the sm_100a decode kernels (kernels.cu). Every launcher queues work on
+// the given stream and returns cudaGetLastError() of its launch.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace bst {
+
+// Kernel classes, reported per class by the engine's timing counters.
+enum KernelClass : int {
+    kEmbed = 0,
+    kLayerNorm = 1,
+    kGemv = 2,
+    kGemm = 3,
+    kAttnDecode = 4,
+    kAttnCombine = 5,
+    kAttnPrefill = 6,
+    kSelectGreedy = 7,
+    kSelectSample = 8,
+    kGather = 9,
+    kHeadLastToken = 10,
+    kMisc = 11,
+    kKernelClassCount = 12,
+};
+
+const char* kernel_class_name(int cls);
+
+// Output stage fused into a projection. `value` = dot(x, w) + bias[n], the order of
+// Linear.forward (torch/Linear.java:30-49): matMul, then the broadcast bias add.
+enum class Epi : int {
+    kStore = 0,        // out[m, n] = value
+    kGelu = 1,         // out[m, n] = gelu(value)                           (Activation GELU)
+    kResidual = 2,     // out[m, n] = out[m, n] + value                     (input.add(attended))
+    kResidualGelu = 3, // out[m, n] = gelu(value + res[m, n])               (charLm back.add(flat))
+    kQkv = 4,          // n < d: q[m, n] = value; else K/V cache at (row[m], slot[m])
+    kLogits = 5,       // out[rowmap[m], n] = value
+};
+
+struct EpiArgs {
+    float* out = nullptr;
+    int ldo = 0;
+    const float* res = nullptr;
+    int ldr = 0;
+    const int* rowmap = nullptr;   // kLogits: destination row; kQkv: cache row
+    const int* slot = nullptr;     // kQkv: cache slot
+    void* k_cache = nullptr;       // kQkv: this layer's K cache [rows][H][S][hd]
+    void* v_cache = nullptr;
+    int d = 0, heads = 0, head_dim = 0, slots = 0;
+    int kv_bf16 = 0;
+};
+
+// Y = X[M, K] * W[N, K]^T + bias with the chosen epilogue. W is float32 or bf16 (w_bf16), K-major.
+cudaError_t launch_linear(cudaStream_t s, const float* x, int ldx, const void* w, int w_bf16,
+                          const float* bias, int M, int N, int K, Epi epi, const EpiArgs& ea);
+// True when launch_linear(M, N, K) uses the small-M GEMV kernel.
+bool linear_uses_gemv(int M, int N, int K);
+
+// x[i] = tok[ids[i]] + pos[positions[i]] for a list of tokens.
+cudaError_t launch_embed_tokens(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
+                                const int* ids, const int* positions, float* x, int count, int d);
+// Decode step begin: for i < R, row = rowmap[i]: slot[i] = len[row]; len[row] += 1;
+// x[i] = tok[next[row]] + pos[slot[i]].
+cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
+                                const int* rowmap, const int* next, int* len, int* slot, float* x,
+                                int R, int d);
+
+// LayerNorm over the last dimension with f64 statistics (nn_ops.rs:168-199).
+cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const float* gamma,
+                             const float* beta, float* y, int ldy, int rows, int d, float eps);
+
+// Split-K decode attention over the cache. q: [R, d]; part: [R, heads, splits, head_dim + 2]
+// holding each split's unnormalised output, running max and sum of exponentials.
+cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
+                               const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
+                               int R, int heads, int head_dim, int slots, float scale, int splits,
+                               int chunk, float* part);
+// Merges the splits: out[i, h*head_dim + e] (out: [R, d]).
+cudaError_t launch_attn_combine(cudaStream_t s, const float* part, int R, int heads, int head_dim,
+                                int splits, float* out);
+// Causal prefill attention for `segments` rows; token t of segment j is packed at
+// seg_start[j] + t and sits in cache slot t of row seg_row[j].
+cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,
+                                const void* v_cache, int kv_bf16, const int* seg_row,
+                                const int* seg_start, const int* seg_len, int segments,
+                                int max_len, int heads, int head_dim, int slots, float scale,
+                                float* out);
+
+// Prefill token list from the device windows: for segment j (row seg_row[j], npad leading PAD
+// ids), tokens window[row][npad + t] at positions t; a segment with no real token gets one PAD id
+// at position 0. Also sets len[row] and the per-token (row, slot) pairs.
+cudaError_t launch_prefill_tokens(cudaStream_t s, const int* window, int W, const int* seg_row,
+                                  const int* seg_npad, const int* seg_start, const int* seg_len,
+                                  int segments, int pad_id, int* ids, int* positions, int* tok_row,
+                                  int* len);
+// Gathers x[seg_start[j] + seg_len[j] - 1] into last[j].
+cudaError_t launch_gather_last(cudaStream_t s, const float* x, const int* seg_start,
+                               const int* seg_len, int segments, int d, float* last);
+// charLm input: x[r, t*d + e] = emb[window[r][t], e] for r < rows.
+cudaError_t launch_window_embed(cudaStream_t s, const int* window, int W, const void* emb,
+                                int w_bf16, int rows, int d, float* x);
+// LastTokenModel head: logits[r, v] = weight[floorMod(window[r][W-1], V), v] + bias[v].
+cudaError_t launch_last_token(cudaStream_t s, const int* window, int W, const float* weight,
+                              const float* bias, int rows, int V, float* logits);
+
+// Token selection plus the step bookkeeping shared by both modes: tokens[r*steps + step] = t,
+// next[r] = t, window[r] shifted left and t appended, and the device step counter advanced once
+// every row is done.
+cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, int V, int W,
+                                 int steps, int* step, int* done, int* tokens, int* next,
+                                 int* window);
+// TextEngine.draw (TextEngine.java:403-427) per row with java.util.Random state rng[r].
+cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, int V, int W,
+                                 int steps, float temperature, int top_k, uint64_t* rng,
+                                 int* step, int* done, int* tokens, int* next, int* window);
+size_t select_sample_smem(int V);
+
+// Sets kernel attributes that must be in place before the first launch on the current device.
+cudaError_t configure_device_kernels();
+
+// Copies this step's logits [rows, V] to history[r][*step][v] (history: [rows, steps, V]).
+cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,
+                                const int* step, float* history);
+
+cudaError_t launch_fill_int(cudaStream_t s, int* p, int value, int count);
+cudaError_t launch_iota(cudaStream_t s, int* p, int count);
+
+}  // namespace bst
