@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""Decode throughput of the CUDA TextEngine on B200.
+
+One step = one TextEngine.generateBatch call over the workload: every row's window is encoded
+(prefill) and then ``steps`` tokens are decoded greedily for every row. The default workload is
+the batch-256 decode of a V4096 / d512 / 6-layer / 8-head / FFN2048 / window-512 padded decoder
+(256-token prompts, 256 new tokens per row, fp32 weights and cache); with N GPUs each rank decodes
+its own 256 rows (batch-sharded, no collective on the data path: weak scaling).
+
+Prints one JSON line (rank 0). ``--impl reference`` times the CPU restatement of the reference
+(full-window recompute per step, as TextEngine does) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+DEFAULT_WORKLOAD = "v4096-d512-l6-w512-b256-greedy"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch1", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        p = json.loads(path.read_text())
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, sm_max, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": sm_max,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(workload, weights_path, threads=None, budget_s=15.0):
+    """The reference's algorithm on the host cores: every step re-runs Module.forward over the
+    full [rows, window] batch (TextEngine.generateBatch, TextEngine.java:232-254) with gemm.rs
+    numerics, on a bounded sample of the workload's rows and steps."""
+    from basalt_b200 import left_pad, synthetic_prompts
+    from oracle import oracle as orc
+
+    if threads:
+        orc.set_threads(threads)
+    m = workload.model
+    oracle = orc.OracleEngine(orc.FAMILY_PADDED_DECODER, m.vocabulary, m.window, m.dimension,
+                              m.layers, m.heads, m.hidden)
+    oracle.load(weights_path)
+    rows = min(4, workload.rows)
+    prompts = synthetic_prompts(workload.prompt_seed, rows, workload.prompt, m.vocabulary)
+    ctx = left_pad(prompts, m.window, m.vocabulary)
+    t0 = time.perf_counter()
+    oracle.generate_batch(ctx, 1)
+    one = time.perf_counter() - t0
+    steps = int(max(1, min(workload.steps, budget_s / max(one, 1e-3))))
+    t0 = time.perf_counter()
+    oracle.generate_batch(ctx, steps)
+    elapsed = time.perf_counter() - t0
+    return {"value": rows * steps / elapsed, "unit": "tokens/s", "cores": orc.threads(),
+            "kind": "port",
+            "sample": f"{rows} rows x {steps} greedy steps of {workload.name}, full-window "
+                      f"recompute per step ({elapsed:.1f} s)"}
+
+
+def run_reference(args, rank, world):
+    from basalt_b200 import config, write_synthetic_weights
+
+    if rank != 0:
+        return
+    workload = config(args.workload)
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "w.bin"
+        write_synthetic_weights(workload.model, path, workload.weight_seed)
+        values = []
+        base = None
+        for i in range(args.warmup + args.steps):
+            base = cpu_baseline(workload, path, budget_s=max(2.0, 60.0 / (args.steps + args.warmup)))
+            if i >= args.warmup:
+                values.append(base["value"])
+    value = float(np.median(values))
+    line = {
+        "impl": "reference", "metric": "decode tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * workload.rows * workload.steps / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": workload.name, "global_batch": workload.rows * args.gpus,
+                   "seq_len": workload.model.window},
+        "cpu_baseline": {**base, "value": value},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+
+    from basalt_b200 import (Basalt, TextEngine, config, left_pad, synthetic_prompts,
+                             write_synthetic_weights)
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    workload = config(args.workload)
+    m = workload.model
+    tmp = tempfile.TemporaryDirectory()
+    wpath = Path(tmp.name) / "w.bin"
+    write_synthetic_weights(m, wpath, workload.weight_seed)
+    engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
+    engine.load(wpath)
+
+    # This rank's shard of the prompts (rows rank*R .. rank*R + R of one seeded draw).
+    R = workload.rows
+    prompts = synthetic_prompts(workload.prompt_seed, R * world, workload.prompt, m.vocabulary)
+    ctx = left_pad(prompts[rank * R:(rank + 1) * R], m.window, m.vocabulary)
+    steps = workload.steps
+
+    stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
+    d_ctx = torch.from_numpy(ctx).to(f"cuda:{local}")
+    d_tok = torch.empty((R, steps), dtype=torch.int32, device=f"cuda:{local}")
+    torch.cuda.synchronize()
+
+    def device_step():
+        engine.generate_device(d_ctx.data_ptr(), R, ctx.shape[1], steps, d_tok.data_ptr())
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    launches0 = engine.stats()["launches"]
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            device_step()
+        stop.record(stream)
+        stop.synchronize()
+    barrier()
+    launches = engine.stats()["launches"] - launches0
+    ms = start.elapsed_time(stop)
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens_per_step = R * steps * world
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+
+    # End to end through the C ABI with host buffers: pinned contexts in, tokens out, every step.
+    h_ctx = torch.from_numpy(ctx).pin_memory()
+    h_tok = torch.empty((R, steps), dtype=torch.int32).pin_memory()
+    from basalt_b200 import _lib
+
+    lib = _lib.load()
+
+    def host_step():
+        code = lib.bst_generate(engine.handle, ctypes.cast(h_ctx.data_ptr(), _lib._i32p), R,
+                                ctx.shape[1], steps, ctypes.cast(h_tok.data_ptr(), _lib._i32p),
+                                _lib.TOKEN_SINK(0), None)
+        if code:
+            raise RuntimeError(_lib.last_error(engine.handle))
+
+    host_step()
+    barrier()
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_stop = torch.cuda.Event(enable_timing=True)
+    e2e_start.record(stream)
+    for _ in range(args.steps):
+        host_step()
+    e2e_stop.record(stream)
+    e2e_stop.synchronize()
+    barrier()
+    e2e_ms = e2e_start.elapsed_time(e2e_stop)
+    if dist:
+        t = torch.tensor([e2e_ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = tokens_per_step * args.steps / (e2e_ms / 1000.0)
+
+    # Prefill alone (one decoded token) vs the whole call: decode-only throughput.
+    d_one = torch.empty((R, 1), dtype=torch.int32, device=f"cuda:{local}")
+    one_start = torch.cuda.Event(enable_timing=True)
+    one_stop = torch.cuda.Event(enable_timing=True)
+    engine.generate_device(d_ctx.data_ptr(), R, ctx.shape[1], 1, d_one.data_ptr())
+    torch.cuda.synchronize()
+    one_start.record(stream)
+    engine.generate_device(d_ctx.data_ptr(), R, ctx.shape[1], 1, d_one.data_ptr())
+    one_stop.record(stream)
+    one_stop.synchronize()
+    prefill_ms = one_start.elapsed_time(one_stop)
+    step_ms = ms / args.steps
+    decode_tps = R * (steps - 1) / max(1e-9, (step_ms - prefill_ms) / 1000.0)
+
+    # Per-kernel device time with CUDA events around each launch (one instrumented step).
+    engine.profile(True)
+    engine.profile_reset()
+    device_step()
+    torch.cuda.synchronize()
+    prof = engine.profile_read()
+    engine.profile(False)
+    top = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    name, k = top
+    hbm, bf16, peak_src = measured_peaks()
+    per_launch_s = k["ms"] / 1000.0 / k["launches"]
+    if name in ("gemm",):
+        achieved = k["flops"] / k["launches"] / per_launch_s / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
+                    "frac": achieved / bf16, "traffic": None, "kernel": name,
+                    "peak_source": peak_src}
+    else:
+        achieved = k["bytes"] / k["launches"] / per_launch_s / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                    "frac": achieved / hbm, "traffic": None, "kernel": name,
+                    "peak_source": peak_src}
+    total_ms = sum(v["ms"] for v in prof.values())
+    kernels = {n: {"launches": v["launches"], "ms": round(v["ms"], 3),
+                   "share": round(v["ms"] / total_ms, 4),
+                   "GB/s": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1) if v["ms"] else None,
+                   "TFLOP/s": round(v["flops"] / (v["ms"] / 1000.0) / 1e12, 2) if v["ms"] else None}
+               for n, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
+
+    line = {
+        "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if m.weight_dtype == "bf16" else "f32",
+        "data": "synthetic: N(0,0.02) weights from java.util.Random(0), prompts from "
+                f"java.util.Random({workload.prompt_seed}).nextInt({m.vocabulary})",
+        "config": {"workload": workload.name, "model": f"padded decoder V{m.vocabulary} "
+                   f"d{m.dimension} L{m.layers} H{m.heads} F{m.hidden} W{m.window}",
+                   "global_batch": R * world, "seq_len": m.window, "prompt": workload.prompt,
+                   "new_tokens": steps, "parallelism": f"batch-sharded x{world}",
+                   "weights": m.weight_dtype, "kv_cache": m.kv_dtype,
+                   "l2": "inputs larger than L2 (KV cache > 1 GB per GPU)"},
+        "prefill_ms": prefill_ms, "decode_tokens_per_s": decode_tps * world,
+        "e2e": {"value": e2e_value, "unit": "tokens/s",
+                "h2d_bytes_per_step": int(ctx.nbytes), "d2h_bytes_per_step": int(R * steps * 4)},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "kernels": kernels,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(workload, wpath)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    engine.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
