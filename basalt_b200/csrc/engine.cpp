@@ -270,15 +270,23 @@ struct Buffer {
     int scope = 0;  // scope depth that owns it; -1 = engine lifetime (weights)
 };
 
+// A projection matrix on the device, K-major [out, in]: `w` in the weight dtype, plus (fp32
+// weights only) its tf32 split w = hi + lo that the tensor-core path multiplies.
+struct Matrix {
+    const void* w = nullptr;
+    const void* hi = nullptr;
+    const void* lo = nullptr;
+};
+
 struct LayerWeights {
-    const void* wqkv = nullptr;  // [3d, d]
+    Matrix wqkv;  // [3d, d]
     const float* bqkv = nullptr;
-    const void* wo = nullptr;    // [d, d]
+    Matrix wo;    // [d, d]
     const float* bo = nullptr;
     const float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
-    const void* w1 = nullptr;    // [F, d]
+    Matrix w1;    // [F, d]
     const float* b1 = nullptr;
-    const void* w2 = nullptr;    // [d, F]
+    Matrix w2;    // [d, F]
     const float* b2 = nullptr;
 };
 
@@ -303,6 +311,8 @@ struct Workspace {
     float *flat = nullptr, *mixed = nullptr;  // charLm
     float* history = nullptr;                 // per-step logits, when requested
     bool has_history = false;
+    void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
+    int* err = nullptr;                       // tensor-core pipeline error code
     void *k_cache = nullptr, *v_cache = nullptr;
     size_t kv_layer_elems = 0;
     uint64_t generation = 0;
@@ -340,9 +350,10 @@ class Engine {
     int scope_depth = 0;
     Buffer weights;
     std::vector<LayerWeights> layers;
-    const void *tok_emb = nullptr, *pos_emb = nullptr, *head_w = nullptr;
+    const void *tok_emb = nullptr, *pos_emb = nullptr;
+    Matrix head_w;
     const float *lnf_g = nullptr, *lnf_b = nullptr, *head_b = nullptr;
-    const void *cl_expand = nullptr, *cl_contract = nullptr;  // charLm
+    Matrix cl_expand, cl_contract;  // charLm
     const float *cl_expand_b = nullptr, *cl_contract_b = nullptr;
     const float *lt_w = nullptr, *lt_b = nullptr;  // LastTokenModel
 
@@ -451,6 +462,8 @@ class Engine {
                  double* scores, float* logits);
     void plan(const std::vector<int32_t>& windows, int rows, int steps,
               std::vector<StepPlan>* plans, int* max_slots, int* max_tokens) const;
+    int linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N, int K,
+               Epi epi, const EpiArgs& ea, const char* what);
     int enqueue_prefill(const StepPlan& p, size_t begin, size_t end);
     int enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens);
     int enqueue_direct(int rows);
@@ -489,35 +502,71 @@ int Engine::upload_weights() {
         return place(std::move(b));
     };
     // Stores `rows_out` rows of length `cols_in` in the weight dtype: element (r, c) of the
-    // device matrix is src(r, c).
-    auto matrix = [&](int64_t rows_out, int64_t cols_in, auto&& src) {
+    // device matrix is src(r, c). With `planes` (projection weights in fp32) the tf32 split
+    // hi = truncate(v), lo = v - hi is stored as well.
+    struct MatIdx {
+        size_t w = 0, hi = 0, lo = 0;
+        bool planes = false;
+    };
+    auto matrix_planes = [&](int64_t rows_out, int64_t cols_in, bool planes, auto&& src) {
         const size_t es = wbf16 ? 2 : 4;
-        std::vector<unsigned char> b(static_cast<size_t>(rows_out * cols_in) * es);
+        const size_t count = static_cast<size_t>(rows_out * cols_in);
+        std::vector<unsigned char> b(count * es);
+        std::vector<unsigned char> hb, lb;
+        const bool split = planes && !wbf16;
+        if (split) {
+            hb.resize(count * 4);
+            lb.resize(count * 4);
+        }
         for (int64_t r = 0; r < rows_out; ++r) {
             for (int64_t c = 0; c < cols_in; ++c) {
                 const float v = src(r, c);
-                const size_t at = static_cast<size_t>(r * cols_in + c) * es;
+                const size_t i = static_cast<size_t>(r * cols_in + c);
                 if (wbf16) {
                     const uint16_t bits = to_bf16_bits(v);
-                    std::memcpy(b.data() + at, &bits, 2);
+                    std::memcpy(b.data() + i * 2, &bits, 2);
                 } else {
-                    std::memcpy(b.data() + at, &v, 4);
+                    std::memcpy(b.data() + i * 4, &v, 4);
+                    if (split) {
+                        uint32_t u;
+                        std::memcpy(&u, &v, 4);
+                        u &= 0xFFFFE000u;
+                        float hi;
+                        std::memcpy(&hi, &u, 4);
+                        const float lo = v - hi;
+                        std::memcpy(hb.data() + i * 4, &hi, 4);
+                        std::memcpy(lb.data() + i * 4, &lo, 4);
+                    }
                 }
             }
         }
-        return place(std::move(b));
+        MatIdx idx;
+        idx.w = place(std::move(b));
+        if (split) {
+            idx.hi = place(std::move(hb));
+            idx.lo = place(std::move(lb));
+            idx.planes = true;
+        }
+        return idx;
+    };
+    auto matrix = [&](int64_t rows_out, int64_t cols_in, auto&& src) {
+        return matrix_planes(rows_out, cols_in, false, src).w;
     };
     auto P = [&](const std::string& n) -> const std::vector<float>& { return values[index.at(n)]; };
     // Linear weight [in, out] -> device [out, in].
     auto transposed = [&](const std::vector<float>& w, int64_t in, int64_t out) {
-        return matrix(out, in, [&](int64_t r, int64_t c) { return w[c * out + r]; });
+        return matrix_planes(out, in, true, [&](int64_t r, int64_t c) { return w[c * out + r]; });
     };
 
     std::vector<size_t> slots_idx;
-    struct LayerIdx { size_t wqkv, bqkv, wo, bo, ln1g, ln1b, ln2g, ln2b, w1, b1, w2, b2; };
+    struct LayerIdx {
+        MatIdx wqkv, wo, w1, w2;
+        size_t bqkv, bo, ln1g, ln1b, ln2g, ln2b, b1, b2;
+    };
     std::vector<LayerIdx> li;
-    size_t i_tok = 0, i_pos = 0, i_lnfg = 0, i_lnfb = 0, i_head = 0, i_headb = 0;
-    size_t i_e1 = 0, i_e1b = 0, i_c = 0, i_cb = 0;
+    size_t i_tok = 0, i_pos = 0, i_lnfg = 0, i_lnfb = 0, i_headb = 0;
+    size_t i_e1b = 0, i_cb = 0, i_lt = 0;
+    MatIdx i_head, i_e1, i_c;
     if (decoder_family(spec.family)) {
         const int64_t emb_rows = static_cast<int64_t>(P("embedding.weight").size()) / d;
         i_tok = matrix(emb_rows, d, [&](int64_t r, int64_t c) { return P("embedding.weight")[r * d + c]; });
@@ -528,7 +577,7 @@ int Engine::upload_weights() {
             const auto& wk = P(p + "attention.key.weight");
             const auto& wv = P(p + "attention.value.weight");
             LayerIdx x{};
-            x.wqkv = matrix(3 * d, d, [&](int64_t r, int64_t c) {
+            x.wqkv = matrix_planes(3 * d, d, true, [&](int64_t r, int64_t c) {
                 const auto& src = r < d ? wq : (r < 2 * d ? wk : wv);
                 return src[c * d + (r % d)];
             });
@@ -564,7 +613,7 @@ int Engine::upload_weights() {
         i_head = transposed(P("param5"), flat, V);
         i_headb = f32(P("param6"));
     } else {
-        i_head = f32(P("param0"));
+        i_lt = f32(P("param0"));
         i_headb = f32(P("param1"));
     }
 
@@ -590,31 +639,40 @@ int Engine::upload_weights() {
 
     auto at = [&](size_t i) { return static_cast<const void*>(static_cast<char*>(weights.ptr) + items[i].offset); };
     auto atf = [&](size_t i) { return static_cast<const float*>(at(i)); };
+    auto atm = [&](const MatIdx& i) {
+        Matrix m;
+        m.w = at(i.w);
+        if (i.planes) {
+            m.hi = at(i.hi);
+            m.lo = at(i.lo);
+        }
+        return m;
+    };
     layers.clear();
     if (decoder_family(spec.family)) {
         tok_emb = at(i_tok);
         pos_emb = at(i_pos);
         for (const auto& x : li) {
             LayerWeights w;
-            w.wqkv = at(x.wqkv); w.bqkv = atf(x.bqkv); w.wo = at(x.wo); w.bo = atf(x.bo);
+            w.wqkv = atm(x.wqkv); w.bqkv = atf(x.bqkv); w.wo = atm(x.wo); w.bo = atf(x.bo);
             w.ln1_g = atf(x.ln1g); w.ln1_b = atf(x.ln1b); w.ln2_g = atf(x.ln2g); w.ln2_b = atf(x.ln2b);
-            w.w1 = at(x.w1); w.b1 = atf(x.b1); w.w2 = at(x.w2); w.b2 = atf(x.b2);
+            w.w1 = atm(x.w1); w.b1 = atf(x.b1); w.w2 = atm(x.w2); w.b2 = atf(x.b2);
             layers.push_back(w);
         }
         lnf_g = atf(i_lnfg);
         lnf_b = atf(i_lnfb);
-        head_w = at(i_head);
+        head_w = atm(i_head);
         head_b = atf(i_headb);
     } else if (spec.family == BST_FAMILY_CHAR_LM) {
         tok_emb = at(i_tok);
-        cl_expand = at(i_e1);
+        cl_expand = atm(i_e1);
         cl_expand_b = atf(i_e1b);
-        cl_contract = at(i_c);
+        cl_contract = atm(i_c);
         cl_contract_b = atf(i_cb);
-        head_w = at(i_head);
+        head_w = atm(i_head);
         head_b = atf(i_headb);
     } else {
-        lt_w = atf(i_head);
+        lt_w = atf(i_lt);
         lt_b = atf(i_headb);
     }
     dirty = false;
@@ -655,6 +713,15 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     add(reinterpret_cast<void**>(&ws.tokens_out), sizeof(int) * static_cast<size_t>(rows) * steps);
     add(reinterpret_cast<void**>(&ws.step), sizeof(int));
     add(reinterpret_cast<void**>(&ws.done), sizeof(int));
+    add(reinterpret_cast<void**>(&ws.err), sizeof(int));
+    {
+        // Split planes for the widest tensor-core operand this run can see.
+        const int kmax = decoder_family(spec.family) ? std::max(d, F)
+                                                     : std::max(W * d, std::max(F, 1));
+        const size_t plane = bst::tc_split_bytes(act_rows, kmax, wbf16);
+        add(&ws.xs_hi, plane);
+        add(&ws.xs_lo, plane);
+    }
     add(reinterpret_cast<void**>(&ws.rng), sizeof(uint64_t) * rows);
     add(reinterpret_cast<void**>(&ws.logits), sizeof(float) * static_cast<size_t>(rows) * V);
     if (history) {
@@ -766,6 +833,36 @@ void Engine::plan(const std::vector<int32_t>& windows, int rows, int steps,
     }
 }
 
+// One projection: GEMV (M <= 8) or tiled FFMA for odd shapes, otherwise split the operand and
+// run the tcgen05 GEMM.
+int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N,
+                   int K, Epi epi, const EpiArgs& ea, const char* what) {
+    const double wb = wbf16 ? 2.0 : 4.0;
+    cudaError_t err;
+    if (bst::tc_usable(M, N, K, wbf16) && (wbf16 || m.hi)) {
+        const double plane = static_cast<double>(bst::tc_split_bytes(M, K, wbf16));
+        err = launch(bst::kSplit, M * K * 4.0 + 2 * plane, 0, 1, [&] {
+            return bst::launch_split_operand(stream, x, ldx, M, K, wbf16, ws.xs_hi, ws.xs_lo);
+        });
+        if (err) return cuda_fail(err, what);
+        const double wbytes = static_cast<double>(N) * K * (wbf16 ? 2.0 : 8.0);
+        err = launch(bst::kGemm, wbytes + 2 * plane + static_cast<double>(M) * N * 4.0,
+                     2.0 * M * N * K, 1, [&] {
+                         return bst::launch_gemm_tc(stream, ws.xs_hi, ws.xs_lo,
+                                                    wbf16 ? m.w : m.hi, m.lo, wbf16, bias, M, N,
+                                                    K, epi, ea, ws.err);
+                     });
+        return err ? cuda_fail(err, what) : BST_OK;
+    }
+    const int cls = bst::linear_uses_gemv(M, N, K) ? bst::kGemv : bst::kMisc;
+    err = launch(cls, static_cast<double>(N) * K * wb + static_cast<double>(M) * K * 4 +
+                          static_cast<double>(M) * N * 4,
+                 2.0 * M * N * K, 1, [&] {
+                     return bst::launch_linear(stream, x, ldx, m.w, wbf16, bias, M, N, K, epi, ea);
+                 });
+    return err ? cuda_fail(err, what) : BST_OK;
+}
+
 int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
     const int segs = static_cast<int>(end - begin);
     std::vector<int> start(segs);
@@ -811,10 +908,6 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         attn_flops += 4.0 * H * hd * n * (n + 1) / 2.0;
         attn_bytes += n * d * (2 * kvb + 8.0);
     }
-    auto gemm_cls = [&](int M, int N, int K) {
-        return bst::linear_uses_gemv(M, N, K) ? bst::kGemv : bst::kGemm;
-    };
-    auto lin_bytes = [&](double M, double N, double K) { return N * K * wb + M * K * 4 + M * N * 4; };
     for (int l = 0; l < L; ++l) {
         const LayerWeights& lw = layers[l];
         st = check(launch(bst::kLayerNorm, T * d * 8.0, 0, 1, [&] {
@@ -834,10 +927,7 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         qkv.head_dim = hd;
         qkv.slots = slots;
         qkv.kv_bf16 = kvbf16;
-        st = check(launch(gemm_cls(T, 3 * d, d), lin_bytes(T, 3 * d, d), 2.0 * T * 3 * d * d, 1, [&] {
-                       return bst::launch_linear(stream, ws.h, d, lw.wqkv, wbf16, lw.bqkv, T, 3 * d,
-                                                 d, Epi::kQkv, qkv);
-                   }), "qkv projection");
+        st = linear(ws.h, d, lw.wqkv, lw.bqkv, T, 3 * d, d, Epi::kQkv, qkv, "qkv projection");
         if (st) return st;
         st = check(launch(bst::kAttnPrefill, attn_bytes, attn_flops, 1, [&] {
                        return bst::launch_attn_prefill(stream, ws.q, qkv.k_cache, qkv.v_cache,
@@ -849,10 +939,7 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         EpiArgs res;
         res.out = ws.x;
         res.ldo = d;
-        st = check(launch(gemm_cls(T, d, d), lin_bytes(T, d, d), 2.0 * T * d * d, 1, [&] {
-                       return bst::launch_linear(stream, ws.att, d, lw.wo, wbf16, lw.bo, T, d, d,
-                                                 Epi::kResidual, res);
-                   }), "output projection");
+        st = linear(ws.att, d, lw.wo, lw.bo, T, d, d, Epi::kResidual, res, "output projection");
         if (st) return st;
         st = check(launch(bst::kLayerNorm, T * d * 8.0, 0, 1, [&] {
                        return bst::launch_layernorm(stream, ws.x, d, lw.ln2_g, lw.ln2_b, ws.h, d, T, d,
@@ -862,15 +949,9 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
-        st = check(launch(gemm_cls(T, F, d), lin_bytes(T, F, d), 2.0 * T * F * d, 1, [&] {
-                       return bst::launch_linear(stream, ws.h, d, lw.w1, wbf16, lw.b1, T, F, d,
-                                                 Epi::kGelu, act);
-                   }), "ffn1");
+        st = linear(ws.h, d, lw.w1, lw.b1, T, F, d, Epi::kGelu, act, "ffn1");
         if (st) return st;
-        st = check(launch(gemm_cls(T, d, F), lin_bytes(T, d, F), 2.0 * T * d * F, 1, [&] {
-                       return bst::launch_linear(stream, ws.ffn, F, lw.w2, wbf16, lw.b2, T, d, F,
-                                                 Epi::kResidual, res);
-                   }), "ffn2");
+        st = linear(ws.ffn, F, lw.w2, lw.b2, T, d, F, Epi::kResidual, res, "ffn2");
         if (st) return st;
     }
     st = check(launch(bst::kGather, segs * d * 8.0, 0, 1, [&] {
@@ -887,10 +968,7 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = ws.seg_row;
-    return check(launch(gemm_cls(segs, V, d), lin_bytes(segs, V, d), 2.0 * segs * V * d, 1, [&] {
-                     return bst::launch_linear(stream, ws.last_h, d, head_w, wbf16, head_b, segs, V,
-                                               d, Epi::kLogits, lg);
-                 }), "head");
+    return linear(ws.last_h, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head");
 }
 
 int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens) {
@@ -910,10 +988,6 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     splits = (max_len + chunk - 1) / chunk;
     if (splits > ws.splits) return fail(BST_PANIC, "decode split count exceeds the workspace");
     auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
-    auto gemm_cls = [&](int M, int N, int K) {
-        return bst::linear_uses_gemv(M, N, K) ? bst::kGemv : bst::kGemm;
-    };
-    auto lin_bytes = [&](double M, double N, double K) { return N * K * wb + M * K * 4 + M * N * 4; };
     int st = check(launch(bst::kEmbed, R * d * (2 * wb + 4.0), 0, 1, [&] {
                        return bst::launch_embed_decode(stream, tok_emb, pos_emb, wbf16, rowmap,
                                                        ws.next, ws.len, ws.slot, ws.x, R, d);
@@ -938,10 +1012,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         qkv.head_dim = hd;
         qkv.slots = slots;
         qkv.kv_bf16 = kvbf16;
-        st = check(launch(gemm_cls(R, 3 * d, d), lin_bytes(R, 3 * d, d), 2.0 * R * 3 * d * d, 1, [&] {
-                       return bst::launch_linear(stream, ws.h, d, lw.wqkv, wbf16, lw.bqkv, R, 3 * d,
-                                                 d, Epi::kQkv, qkv);
-                   }), "qkv projection");
+        st = linear(ws.h, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv, "qkv projection");
         if (st) return st;
         const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0;
         st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * sum_len * d, 1, [&] {
@@ -957,10 +1028,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         EpiArgs res;
         res.out = ws.x;
         res.ldo = d;
-        st = check(launch(gemm_cls(R, d, d), lin_bytes(R, d, d), 2.0 * R * d * d, 1, [&] {
-                       return bst::launch_linear(stream, ws.att, d, lw.wo, wbf16, lw.bo, R, d, d,
-                                                 Epi::kResidual, res);
-                   }), "output projection");
+        st = linear(ws.att, d, lw.wo, lw.bo, R, d, d, Epi::kResidual, res, "output projection");
         if (st) return st;
         st = check(launch(bst::kLayerNorm, R * d * 8.0, 0, 1, [&] {
                        return bst::launch_layernorm(stream, ws.x, d, lw.ln2_g, lw.ln2_b, ws.h, d, R, d,
@@ -970,15 +1038,9 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
-        st = check(launch(gemm_cls(R, F, d), lin_bytes(R, F, d), 2.0 * R * F * d, 1, [&] {
-                       return bst::launch_linear(stream, ws.h, d, lw.w1, wbf16, lw.b1, R, F, d,
-                                                 Epi::kGelu, act);
-                   }), "ffn1");
+        st = linear(ws.h, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1");
         if (st) return st;
-        st = check(launch(gemm_cls(R, d, F), lin_bytes(R, d, F), 2.0 * R * d * F, 1, [&] {
-                       return bst::launch_linear(stream, ws.ffn, F, lw.w2, wbf16, lw.b2, R, d, F,
-                                                 Epi::kResidual, res);
-                   }), "ffn2");
+        st = linear(ws.ffn, F, lw.w2, lw.b2, R, d, F, Epi::kResidual, res, "ffn2");
         if (st) return st;
     }
     st = check(launch(bst::kLayerNorm, R * d * 8.0, 0, 1, [&] {
@@ -990,10 +1052,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = rowmap;
-    return check(launch(gemm_cls(R, V, d), lin_bytes(R, V, d), 2.0 * R * V * d, 1, [&] {
-                     return bst::launch_linear(stream, ws.h, d, head_w, wbf16, head_b, R, V, d,
-                                               Epi::kLogits, lg);
-                 }), "head");
+    return linear(ws.h, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head");
 }
 
 // Families without a cache: the whole window is the input every step.
@@ -1008,10 +1067,6 @@ int Engine::enqueue_direct(int rows) {
     // Zoo.WindowedLanguageModel.forward (zoo/Zoo.java:155-168).
     const double wb = wbf16 ? 2.0 : 4.0;
     const int flat = W * d;
-    auto gemm_cls = [&](int M, int N, int K) {
-        return bst::linear_uses_gemv(M, N, K) ? bst::kGemv : bst::kGemm;
-    };
-    auto lin_bytes = [&](double M, double N, double K) { return N * K * wb + M * K * 4 + M * N * 4; };
     int st = check(launch(bst::kEmbed, rows * flat * (wb + 4.0), 0, 1, [&] {
                        return bst::launch_window_embed(stream, ws.window, W, tok_emb, wbf16, rows,
                                                        d, ws.flat);
@@ -1020,29 +1075,20 @@ int Engine::enqueue_direct(int rows) {
     EpiArgs g;
     g.out = ws.ffn;
     g.ldo = F;
-    st = check(launch(gemm_cls(rows, F, flat), lin_bytes(rows, F, flat), 2.0 * rows * F * flat, 1, [&] {
-                   return bst::launch_linear(stream, ws.flat, flat, cl_expand, wbf16, cl_expand_b,
-                                             rows, F, flat, Epi::kGelu, g);
-               }), "expand");
+    st = linear(ws.flat, flat, cl_expand, cl_expand_b, rows, F, flat, Epi::kGelu, g, "expand");
     if (st) return st;
     EpiArgs rg;
     rg.out = ws.mixed;
     rg.ldo = flat;
     rg.res = ws.flat;
     rg.ldr = flat;
-    st = check(launch(gemm_cls(rows, flat, F), lin_bytes(rows, flat, F), 2.0 * rows * flat * F, 1, [&] {
-                   return bst::launch_linear(stream, ws.ffn, F, cl_contract, wbf16, cl_contract_b,
-                                             rows, flat, F, Epi::kResidualGelu, rg);
-               }), "contract");
+    st = linear(ws.ffn, F, cl_contract, cl_contract_b, rows, flat, F, Epi::kResidualGelu, rg, "contract");
     if (st) return st;
     EpiArgs lg;
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = ws.rowmap_all;
-    return check(launch(gemm_cls(rows, V, flat), lin_bytes(rows, V, flat), 2.0 * rows * V * flat, 1, [&] {
-                     return bst::launch_linear(stream, ws.mixed, flat, head_w, wbf16, head_b, rows,
-                                               V, flat, Epi::kLogits, lg);
-                 }), "head");
+    return linear(ws.mixed, flat, head_w, head_b, rows, V, flat, Epi::kLogits, lg, "head");
 }
 
 int Engine::enqueue_select(Mode mode, int rows, int steps, float temperature, int top_k,
@@ -1089,6 +1135,7 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
                                       cudaMemcpyHostToDevice, stream);
     if (!err) err = cudaMemsetAsync(ws.step, 0, sizeof(int), stream);
     if (!err) err = cudaMemsetAsync(ws.done, 0, sizeof(int), stream);
+    if (!err) err = cudaMemsetAsync(ws.err, 0, sizeof(int), stream);
     if (!err) err = cudaMemsetAsync(ws.len, 0, sizeof(int) * rows, stream);
     if (!err && mode == Mode::kSample) {
         std::vector<uint64_t> states(rows);
@@ -1203,6 +1250,14 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
         }
     }
     (void)total_rows;
+    int pipeline_error = 0;
+    err = cudaMemcpyAsync(&pipeline_error, ws.err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (!err) err = cudaStreamSynchronize(stream);
+    if (err) return cuda_fail(err, "reading the pipeline status");
+    if (pipeline_error) {
+        return fail(BST_PANIC, "a tensor-core GEMM pipeline wait timed out (stage " +
+                                   std::to_string(pipeline_error) + ")");
+    }
     if (mode == Mode::kScores) {
         std::vector<float> logits(static_cast<size_t>(rows) * V);
         err = cudaMemcpyAsync(logits.data(), ws.logits, sizeof(float) * logits.size(),

@@ -1,0 +1,54 @@
+// Epilogue stages shared by the projection kernels (kernels.cu, gemm_tc.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "kernels.h"
+
+namespace bst {
+
+// gelu_forward (nn_ops.rs:130-137): 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))), evaluated in
+// f32 in the reference's operation order without contraction.
+__device__ __forceinline__ float gelu_ref(float v) {
+    const float c = __fsqrt_rn(__fdiv_rn(2.0f, 3.14159274101257324f));
+    const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v);
+    const float inner = __fmul_rn(c, __fadd_rn(v, cube));
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <Epi E>
+__device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float v) {
+    if constexpr (E == Epi::kStore) {
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] = v;
+    } else if constexpr (E == Epi::kGelu) {
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] = gelu_ref(v);
+    } else if constexpr (E == Epi::kResidual) {
+        float* p = ea.out + static_cast<size_t>(m) * ea.ldo + n;
+        *p = __fadd_rn(*p, v);
+    } else if constexpr (E == Epi::kResidualGelu) {
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] =
+            gelu_ref(__fadd_rn(v, ea.res[static_cast<size_t>(m) * ea.ldr + n]));
+    } else if constexpr (E == Epi::kQkv) {
+        if (n < ea.d) {
+            ea.out[static_cast<size_t>(m) * ea.ldo + n] = v;
+        } else {
+            const int which = n / ea.d;
+            const int j = n - which * ea.d;
+            const int h = j / ea.head_dim;
+            const int e = j - h * ea.head_dim;
+            const size_t idx =
+                ((static_cast<size_t>(ea.rowmap[m]) * ea.heads + h) * ea.slots + ea.slot[m]) *
+                    ea.head_dim + e;
+            void* base = which == 1 ? ea.k_cache : ea.v_cache;
+            if (ea.kv_bf16) {
+                static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+            } else {
+                static_cast<float*>(base)[idx] = v;
+            }
+        }
+    } else if constexpr (E == Epi::kLogits) {
+        ea.out[static_cast<size_t>(ea.rowmap[m]) * ea.ldo + n] = v;
+    }
+}
+
+}  // namespace bst

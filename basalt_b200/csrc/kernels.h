@@ -21,7 +21,8 @@ enum KernelClass : int {
     kGather = 9,
     kHeadLastToken = 10,
     kMisc = 11,
-    kKernelClassCount = 12,
+    kSplit = 12,
+    kKernelClassCount = 13,
 };
 
 const char* kernel_class_name(int cls);
@@ -117,6 +118,21 @@ size_t select_sample_smem(int V);
 
 // Sets kernel attributes that must be in place before the first launch on the current device.
 cudaError_t configure_device_kernels();
+
+// ---- tensor-core projections (gemm_tc.cu) ----
+cudaError_t configure_tc_kernels();
+// True when Y = X W^T of this shape runs on tcgen05 (M > 8; K aligned for TMA).
+bool tc_usable(int M, int N, int K, int w_bf16);
+// Bytes of one split plane for an [M, K] operand.
+size_t tc_split_bytes(int M, int K, int w_bf16);
+// X -> (hi, lo) planes: tf32 truncation and fp32 remainder, or two bf16 planes (w_bf16).
+cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M, int K, int w_bf16,
+                                 void* hi, void* lo);
+// Y = Xh*Wh + Xh*Wl + Xl*Wh (fp32 weights: w = Wh, w_lo = Wl) or Xh*W + Xl*W (bf16 weights),
+// plus bias, through the epilogue. *err receives a non-zero code if a pipeline wait timed out.
+cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, const void* w,
+                           const void* w_lo, int w_bf16, const float* bias, int M, int N, int K,
+                           Epi epi, const EpiArgs& ea, int* err);
 
 // Copies this step's logits [rows, V] to history[r][*step][v] (history: [rows, steps, V]).
 cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,

@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true")
+    ap.add_argument("--rows", type=int, default=0, help="override the workload's rows per GPU")
+    ap.add_argument("--new-tokens", type=int, default=0, help="override tokens decoded per row")
     return ap.parse_args()
 
 
@@ -195,6 +197,11 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     workload = config(args.workload)
+    if args.rows or args.new_tokens:
+        from dataclasses import replace
+
+        workload = replace(workload, rows=args.rows or workload.rows,
+                           steps=args.new_tokens or workload.steps)
     m = workload.model
     tmp = tempfile.TemporaryDirectory()
     wpath = Path(tmp.name) / "w.bin"
