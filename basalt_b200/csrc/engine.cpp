@@ -1348,6 +1348,12 @@ int Engine::run(Mode mode, const int32_t* contexts, int32_t rows, int32_t length
     return BST_OK;
 }
 
+}  // namespace
+
+void bst::set_thread_error(const std::string& message) { t_last_error = message; }
+
+namespace {
+
 int set_error(const std::shared_ptr<Engine>& e, int code) {
     if (code != BST_OK && e) t_last_error = e->error;
     return code;
@@ -1440,7 +1446,7 @@ int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine
         }
         err = cudaSetDevice(device);
         if (!err) err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
-        if (!err) err = bst::configure_device_kernels();
+        if (!err) err = bst::configure_device_kernels_once(device);
         if (err) {
             cudaGetLastError();
             t_last_error = std::string("cannot initialise the device: ") + cudaGetErrorString(err);

@@ -17,6 +17,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace bst {
 
 const char* kernel_class_name(int cls) {
@@ -1054,6 +1056,16 @@ cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, i
     if (rows <= 0) return cudaSuccess;
     k_stash_logits<<<dim3((V + 255) / 256, rows), 256, 0, s>>>(logits, V, steps, step, history);
     return cudaGetLastError();
+}
+
+cudaError_t configure_device_kernels_once(int device) {
+    static std::mutex mu;
+    static uint64_t done = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (device >= 0 && device < 64 && (done >> device) & 1ull) return cudaSuccess;
+    const cudaError_t err = configure_device_kernels();
+    if (err == cudaSuccess && device >= 0 && device < 64) done |= 1ull << device;
+    return err;
 }
 
 cudaError_t launch_fill_int(cudaStream_t s, int* p, int value, int count) {

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace bst {
 
 // Kernel classes, reported per class by the engine's timing counters.
@@ -118,6 +120,10 @@ size_t select_sample_smem(int V);
 
 // Sets kernel attributes that must be in place before the first launch on the current device.
 cudaError_t configure_device_kernels();
+// configure_device_kernels once per device for the process (the device must be current).
+cudaError_t configure_device_kernels_once(int device);
+// Message returned by bst_last_error(0) on this thread.
+void set_thread_error(const std::string& message);
 
 // ---- tensor-core projections (gemm_tc.cu) ----
 cudaError_t configure_tc_kernels();

@@ -158,6 +158,14 @@ int32_t bst_profile_reset(bst_engine engine);
 int32_t bst_profile_read(bst_engine engine, int32_t kernel_class, char* name, int32_t capacity,
                          int64_t* launches, double* milliseconds, double* bytes, double* flops);
 
+/* Tensor.matMul (torch/Tensor.java:214-227) -> gemm::matmul (native/src/gemm.rs:42-74) on device
+ * buffers: C[m, n] = A[m, k] * B[k, n], row-major float32, C overwritten. Runs on `device`, queued
+ * on `stream` (a cudaStream_t; NULL is the legacy default stream) and returns once C is complete.
+ * m <= 8 uses the GEMV kernel, larger m the tcgen05 GEMM (3xTF32). Temporaries (B transposed and
+ * the split operand planes) come from the stream-ordered allocator. Errors: bst_last_error(0). */
+int32_t bst_matmul(int32_t device, void* stream, const float* a, const float* b, float* c,
+                   int64_t m, int64_t k, int64_t n);
+
 /* Message of the last failure on this engine (engine 0: on this thread). */
 int32_t bst_last_error(bst_engine engine, char* buffer, int32_t capacity);
 
