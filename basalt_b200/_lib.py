@@ -96,6 +96,9 @@ SIGNATURES = {
     "bst_matmul": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                     ctypes.c_int64, ctypes.c_int64]),
+    "bst_matmul_static": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_int64]),
     "bst_last_error": (ctypes.c_int32, [_u64, ctypes.c_char_p, ctypes.c_int32]),
     "bst_write_synthetic_weights": (ctypes.c_int32, [_P(ModelSpecStruct), ctypes.c_char_p,
                                                      ctypes.c_int64, ctypes.c_double]),

@@ -166,6 +166,15 @@ int32_t bst_profile_read(bst_engine engine, int32_t kernel_class, char* name, in
 int32_t bst_matmul(int32_t device, void* stream, const float* a, const float* b, float* c,
                    int64_t m, int64_t k, int64_t n);
 
+/* bst_matmul that allocates no device memory, for callers that may not call cudaMalloc while
+ * they run. No counterpart in the reference. Temporaries come from a 16 MiB scratch array built
+ * into the library (held on every GPU that loads it until exit); problems whose scratch does not
+ * fit are rejected with BST_SHAPE. The first call on a device looks up that array's device address
+ * and should come before any stream capture. Calls share the array: work from calls that overlaps
+ * on the GPU races, so such calls must be serialised by the caller. */
+int32_t bst_matmul_static(int32_t device, void* stream, const float* a, const float* b, float* c,
+                          int64_t m, int64_t k, int64_t n);
+
 /* Message of the last failure on this engine (engine 0: on this thread). */
 int32_t bst_last_error(bst_engine engine, char* buffer, int32_t capacity);
 
