@@ -313,6 +313,7 @@ struct Workspace {
     bool has_history = false;
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
     int* err = nullptr;                       // tensor-core pipeline error code
+    float* tc_part = nullptr;                 // split-K partial products
     void *k_cache = nullptr, *v_cache = nullptr;
     size_t kv_layer_elems = 0;
     uint64_t generation = 0;
@@ -721,6 +722,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
         const size_t plane = bst::tc_split_bytes(act_rows, kmax, wbf16);
         add(&ws.xs_hi, plane);
         add(&ws.xs_lo, plane);
+        add(reinterpret_cast<void**>(&ws.tc_part), bst::tc_part_bytes_max());
     }
     add(reinterpret_cast<void**>(&ws.rng), sizeof(uint64_t) * rows);
     add(reinterpret_cast<void**>(&ws.logits), sizeof(float) * static_cast<size_t>(rows) * V);
@@ -846,11 +848,15 @@ int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, 
         });
         if (err) return cuda_fail(err, what);
         const double wbytes = static_cast<double>(N) * K * (wbf16 ? 2.0 : 8.0);
+        // A split-K GEMM is two kernels (partial products, then the ordered fix-up).
+        const int kernels =
+            bst::tc_plan(M, N, K, wbf16, bst::tc_part_bytes_max(), nullptr) > 1 ? 2 : 1;
         err = launch(bst::kGemm, wbytes + 2 * plane + static_cast<double>(M) * N * 4.0,
-                     2.0 * M * N * K, 1, [&] {
+                     2.0 * M * N * K, kernels, [&] {
                          return bst::launch_gemm_tc(stream, ws.xs_hi, ws.xs_lo,
                                                     wbf16 ? m.w : m.hi, m.lo, wbf16, bias, M, N,
-                                                    K, epi, ea, ws.err);
+                                                    K, epi, ea, ws.err, ws.tc_part,
+                                                    bst::tc_part_bytes_max());
                      });
         return err ? cuda_fail(err, what) : BST_OK;
     }

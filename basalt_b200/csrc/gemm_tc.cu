@@ -161,7 +161,8 @@ template <int FMT, int BN, Epi E>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
     const __grid_constant__ CUtensorMap a0, const __grid_constant__ CUtensorMap a1,
     const __grid_constant__ CUtensorMap b0, const __grid_constant__ CUtensorMap b1,
-    const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err) {
+    const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err, int splits,
+    float* __restrict__ part) {
     using C = Config<FMT, BN>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -173,7 +174,11 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int k_tiles = (K + C::kElemsPerRow - 1) / C::kElemsPerRow;
+    // Split-K: this CTA accumulates k-tiles [kt0, kt1) (the host makes every split non-empty).
+    const int k_total = (K + C::kElemsPerRow - 1) / C::kElemsPerRow;
+    const int per = (k_total + splits - 1) / splits;
+    const int kt0 = blockIdx.z * per;
+    const int k_tiles = min(k_total, kt0 + per) - kt0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
@@ -208,7 +213,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
                 ok = mbar_wait(&empty[s], phase ^ 1, err, 1);
                 if (!ok) break;
                 mbar_expect_tx(&full[s], C::kStageBytes);
-                const int kx = kt * C::kElemsPerRow;
+                const int kx = (kt0 + kt) * C::kElemsPerRow;
                 tma_load_2d(&a0, &full[s], stage_a(s, 0), kx, m0);
                 tma_load_2d(&a1, &full[s], stage_a(s, 1), kx, m0);
                 tma_load_2d(&b0, &full[s], stage_b(s, 0), kx, n0);
@@ -254,19 +259,37 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
         const int quarter = warp & 3;
         const bool ok = mbar_wait(acc_full, 0, err, 3);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (ok) {
-            const int m = m0 + quarter * 32 + lane;
+        // Stage the 128 x BN tile through shared memory (the drained pipeline ring), so the
+        // global traffic below is row-coalesced.
+        float* tile = reinterpret_cast<float*>(base);
+        constexpr int LD = BN + 1;
+        if (__all_sync(0xffffffffu, ok)) {
+            const int r = quarter * 32 + lane;
             const uint32_t row_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
             for (int c = 0; c < BN; c += 16) {
                 float v[16];
                 tmem_ld16(row_addr + c, v);
-                if (m < M) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int n = n0 + c + j;
-                        if (n < N) epi_apply<E>(ea, m, n, bias ? __fadd_rn(v[j], bias[n]) : v[j]);
-                    }
+                for (int j = 0; j < 16; ++j) tile[r * LD + c + j] = v[j];
+            }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int t = threadIdx.x - 64;
+        if (splits > 1) {
+            float* out = part + static_cast<size_t>(blockIdx.z) * M * N;
+            for (int e = t; e < BM * BN; e += 128) {
+                const int r = e / BN, c = e - r * BN;
+                const int m = m0 + r, n = n0 + c;
+                if (m < M && n < N) out[static_cast<size_t>(m) * N + n] = tile[r * LD + c];
+            }
+        } else {
+            for (int e = t; e < BM * BN; e += 128) {
+                const int r = e / BN, c = e - r * BN;
+                const int m = m0 + r, n = n0 + c;
+                if (m < M && n < N) {
+                    const float v = tile[r * LD + c];
+                    epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, bias[n]) : v);
                 }
             }
         }
@@ -276,6 +299,21 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
     if (warp == 1) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(C::kTmemCols));
+    }
+}
+
+// Split-K fix-up: out = sum over splits z = 0..S-1 (in that order) of part[z], then bias and the
+// epilogue. Deterministic; coalesced over n.
+template <Epi E>
+__global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int M, int N,
+                                const float* __restrict__ bias, EpiArgs ea) {
+    const size_t total = static_cast<size_t>(M) * N;
+    for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float v = 0.0f;
+        for (int z = 0; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
+        const int m = static_cast<int>(e / N), n = static_cast<int>(e % N);
+        epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, bias[n]) : v);
     }
 }
 
@@ -339,27 +377,38 @@ cudaError_t make_map(CUtensorMap* map, const void* ptr, int rows, int K, bool bf
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+struct SplitK {
+    int splits = 1;
+    float* part = nullptr;
+};
+
 template <int FMT, int BN, Epi E>
 cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1,
                          const CUtensorMap& b0, const CUtensorMap& b1, const float* bias, int M,
-                         int N, int K, const EpiArgs& ea, int* err) {
+                         int N, int K, const EpiArgs& ea, int* err, const SplitK& sk) {
     using C = Config<FMT, BN>;
-    const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    k_gemm_tc<FMT, BN, E><<<grid, kThreads, C::kSmem, s>>>(a0, a1, b0, b1, bias, M, N, K, ea, err);
+    const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits);
+    k_gemm_tc<FMT, BN, E><<<grid, kThreads, C::kSmem, s>>>(a0, a1, b0, b1, bias, M, N, K, ea, err,
+                                                           sk.splits, sk.part);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || sk.splits == 1) return e;
+    const size_t total = static_cast<size_t>(M) * N;
+    const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
+    k_splitk_reduce<E><<<blocks, 256, 0, s>>>(sk.part, sk.splits, M, N, bias, ea);
     return cudaGetLastError();
 }
 
 template <int FMT, int BN>
 cudaError_t launch_epi(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1,
                        const CUtensorMap& b0, const CUtensorMap& b1, const float* bias, int M,
-                       int N, int K, Epi epi, const EpiArgs& ea, int* err) {
+                       int N, int K, Epi epi, const EpiArgs& ea, int* err, const SplitK& sk) {
     switch (epi) {
-        case Epi::kStore: return launch_typed<FMT, BN, Epi::kStore>(s, a0, a1, b0, b1, bias, M, N, K, ea, err);
-        case Epi::kGelu: return launch_typed<FMT, BN, Epi::kGelu>(s, a0, a1, b0, b1, bias, M, N, K, ea, err);
-        case Epi::kResidual: return launch_typed<FMT, BN, Epi::kResidual>(s, a0, a1, b0, b1, bias, M, N, K, ea, err);
-        case Epi::kResidualGelu: return launch_typed<FMT, BN, Epi::kResidualGelu>(s, a0, a1, b0, b1, bias, M, N, K, ea, err);
-        case Epi::kQkv: return launch_typed<FMT, BN, Epi::kQkv>(s, a0, a1, b0, b1, bias, M, N, K, ea, err);
-        case Epi::kLogits: return launch_typed<FMT, BN, Epi::kLogits>(s, a0, a1, b0, b1, bias, M, N, K, ea, err);
+        case Epi::kStore: return launch_typed<FMT, BN, Epi::kStore>(s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk);
+        case Epi::kGelu: return launch_typed<FMT, BN, Epi::kGelu>(s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk);
+        case Epi::kResidual: return launch_typed<FMT, BN, Epi::kResidual>(s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk);
+        case Epi::kResidualGelu: return launch_typed<FMT, BN, Epi::kResidualGelu>(s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk);
+        case Epi::kQkv: return launch_typed<FMT, BN, Epi::kQkv>(s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk);
+        case Epi::kLogits: return launch_typed<FMT, BN, Epi::kLogits>(s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk);
     }
     return cudaErrorInvalidValue;
 }
@@ -421,15 +470,44 @@ cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M,
     return cudaGetLastError();
 }
 
+int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out) {
+    // Narrow tiles when the grid would not cover the SMs, then split K until it does (one wave);
+    // each split keeps at least two k-tiles.
+    const int tiles_m = (M + BM - 1) / BM;
+    const int bn = ((N + 127) / 128) * tiles_m >= 148 ? 128 : 64;
+    const int tiles = ((N + bn - 1) / bn) * tiles_m;
+    const int k_tiles = (K + (w_bf16 ? 63 : 31)) / (w_bf16 ? 64 : 32);
+    int splits = 1;
+    if (tiles < 148) {
+        splits = std::min((148 + tiles - 1) / tiles, std::max(1, k_tiles / 2));
+        const size_t per_split = static_cast<size_t>(M) * N * sizeof(float);
+        while (splits > 1 && per_split * splits > part_bytes) --splits;
+        if (splits > 1) {
+            const int per = (k_tiles + splits - 1) / splits;
+            splits = (k_tiles + per - 1) / per;  // no empty split
+        }
+    }
+    if (bn_out) *bn_out = bn;
+    return splits;
+}
+
+size_t tc_part_bytes_max() { return static_cast<size_t>(296) * BM * 64 * sizeof(float); }
+
+size_t tc_part_bytes(int M, int N, int K, int w_bf16) {
+    const int splits = tc_plan(M, N, K, w_bf16, tc_part_bytes_max(), nullptr);
+    return splits > 1 ? static_cast<size_t>(splits) * M * N * sizeof(float) : 0;
+}
+
 cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, const void* w,
                            const void* w_lo, int w_bf16, const float* bias, int M, int N, int K,
-                           Epi epi, const EpiArgs& ea, int* err) {
+                           Epi epi, const EpiArgs& ea, int* err, float* part, size_t part_bytes) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     cudaError_t e = encoder();
     if (e != cudaSuccess) return e;
-    // Narrow tiles when the grid would not cover the SMs.
-    const int tiles_m = (M + BM - 1) / BM;
-    const int bn = ((N + 127) / 128) * tiles_m >= 148 ? 128 : 64;
+    int bn = 64;
+    SplitK sk;
+    sk.splits = tc_plan(M, N, K, w_bf16, part ? part_bytes : 0, &bn);
+    sk.part = part;
     CUtensorMap a0, a1, b0, b1;
     if ((e = make_map(&a0, x_hi, M, K, w_bf16, BM)) != cudaSuccess) return e;
     if ((e = make_map(&a1, x_lo, M, K, w_bf16, BM)) != cudaSuccess) return e;
@@ -440,11 +518,11 @@ cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, c
         return e;
     }
     if (w_bf16) {
-        return bn == 128 ? launch_epi<1, 128>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err)
-                         : launch_epi<1, 64>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err);
+        return bn == 128 ? launch_epi<1, 128>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err, sk)
+                         : launch_epi<1, 64>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err, sk);
     }
-    return bn == 128 ? launch_epi<2, 128>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err)
-                     : launch_epi<2, 64>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err);
+    return bn == 128 ? launch_epi<2, 128>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err, sk)
+                     : launch_epi<2, 64>(s, a0, a1, b0, b1, bias, M, N, K, epi, ea, err, sk);
 }
 
 }  // namespace bst

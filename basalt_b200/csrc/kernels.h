@@ -136,9 +136,18 @@ cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M,
                                  void* hi, void* lo);
 // Y = Xh*Wh + Xh*Wl + Xl*Wh (fp32 weights: w = Wh, w_lo = Wl) or Xh*W + Xl*W (bf16 weights),
 // plus bias, through the epilogue. *err receives a non-zero code if a pipeline wait timed out.
+// When the output tiles do not fill the SMs, K is split across CTAs: each writes its fp32 partial
+// product to part[z] ([splits][M][N], part_bytes of room) and a second kernel sums the splits in
+// order and runs the epilogue (deterministic). With part == nullptr the GEMM never splits.
 cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, const void* w,
                            const void* w_lo, int w_bf16, const float* bias, int M, int N, int K,
-                           Epi epi, const EpiArgs& ea, int* err);
+                           Epi epi, const EpiArgs& ea, int* err, float* part = nullptr,
+                           size_t part_bytes = 0);
+// Split count and tile width launch_gemm_tc chooses for this shape and scratch.
+int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out);
+// Partial scratch that lets every shape reach one full wave of CTAs, and what one shape needs.
+size_t tc_part_bytes_max();
+size_t tc_part_bytes(int M, int N, int K, int w_bf16);
 
 // Copies this step's logits [rows, V] to history[r][*step][v] (history: [rows, steps, V]).
 cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,

@@ -46,11 +46,18 @@ __global__ void k_transpose_split(const float* __restrict__ b, int k, int n,
 
 }  // namespace
 
+namespace {
+// Partial-product bytes the split-K plan of this shape needs (0 when it does not split).
+size_t split_part_bytes(int64_t m, int64_t k, int64_t n) {
+    return tc_part_bytes(static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), 0);
+}
+}  // namespace
+
 size_t matmul_scratch_bytes(int64_t m, int64_t k, int64_t n) {
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
     if (tc_usable(static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), 0)) {
         return up(sizeof(int)) + 2 * up(static_cast<size_t>(m) * k * 4) +
-               2 * up(static_cast<size_t>(n) * k * 4);
+               2 * up(static_cast<size_t>(n) * k * 4) + up(split_part_bytes(m, k, n));
     }
     return up(sizeof(int)) + up(static_cast<size_t>(n) * k * 4);
 }
@@ -77,10 +84,18 @@ int32_t matmul_with_scratch(cudaStream_t s, const float* a, const float* b, floa
         float* bh = reinterpret_cast<float*>(p);
         p += up(static_cast<size_t>(n) * k * 4);
         float* bl = reinterpret_cast<float*>(p);
-        k_transpose_split<<<tgrid, tblock, 0, s>>>(b, K, N, nullptr, bh, bl);
-        e = cudaGetLastError();
+        p += up(static_cast<size_t>(n) * k * 4);
+        float* part = reinterpret_cast<float*>(p);
+        const size_t part_bytes = split_part_bytes(m, k, n);
+        if (!e) {
+            k_transpose_split<<<tgrid, tblock, 0, s>>>(b, K, N, nullptr, bh, bl);
+            e = cudaGetLastError();
+        }
         if (!e) e = launch_split_operand(s, a, K, M, K, 0, ah, al);
-        if (!e) e = launch_gemm_tc(s, ah, al, bh, bl, 0, nullptr, M, N, K, Epi::kStore, ea, err);
+        if (!e) {
+            e = launch_gemm_tc(s, ah, al, bh, bl, 0, nullptr, M, N, K, Epi::kStore, ea, err,
+                               part_bytes ? part : nullptr, part_bytes);
+        }
     } else if (!e) {
         float* bt = reinterpret_cast<float*>(p);
         k_transpose_split<<<tgrid, tblock, 0, s>>>(b, K, N, bt, nullptr, nullptr);

@@ -17,9 +17,9 @@
 // first call on a device before any stream capture.
 //
 // All calls share the one array and it keeps whatever the last call left in it; the part that must
-// start at zero (the pipeline error word) is cleared by every call. Calls whose work overlaps on
-// the GPU (different streams, or different host threads on the same device) race on the scratch
-// and must be serialised by the caller.
+// start at zero (the pipeline error word) is cleared by every call.
+// Calls whose work overlaps on the GPU (different streams, or different host threads on the same
+// device) race on the scratch and must be serialised by the caller.
 
 #include <cuda_runtime.h>
 

@@ -29,6 +29,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 DEFAULT_WORKLOAD = "v4096-d512-l6-w512-b256-greedy"
+BATCH1_WORKLOAD = "v8192-d768-l12-w1024-b1-greedy-bf16w"
 
 
 def parse():
@@ -141,6 +142,80 @@ def cpu_baseline(workload, weights_path, threads=None, budget_s=15.0):
             "kind": "port",
             "sample": f"{rows} rows x {steps} greedy steps of {workload.name}, full-window "
                       f"recompute per step ({elapsed:.1f} s)"}
+
+
+def profile_summary(engine, run):
+    """Per-kernel device time of one call of `run`, CUDA events around every launch."""
+    import torch
+
+    engine.profile(True)
+    engine.profile_reset()
+    run()
+    torch.cuda.synchronize()
+    prof = engine.profile_read()
+    engine.profile(False)
+    total_ms = sum(v["ms"] for v in prof.values()) or 1.0
+    kernels = {n: {"launches": v["launches"], "ms": round(v["ms"], 3),
+                   "share": round(v["ms"] / total_ms, 4),
+                   "GB/s": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1) if v["ms"] else None,
+                   "TFLOP/s": round(v["flops"] / (v["ms"] / 1000.0) / 1e12, 2) if v["ms"] else None}
+               for n, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
+    return prof, kernels
+
+
+def batch1(local, steps, warmup):
+    """Single-stream latency: batch 1, 512-token prompt, 512 greedy tokens (bf16 weights)."""
+    import torch
+
+    from basalt_b200 import (Basalt, TextEngine, config, left_pad, synthetic_prompts,
+                             write_synthetic_weights)
+
+    w = config(BATCH1_WORKLOAD)
+    m = w.model
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "w.bin"
+        write_synthetic_weights(m, path, w.weight_seed)
+        engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
+        engine.load(path)
+    ctx = left_pad(synthetic_prompts(w.prompt_seed, 1, w.prompt, m.vocabulary), m.window,
+                   m.vocabulary)
+    stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
+    d_ctx = torch.from_numpy(ctx).to(f"cuda:{local}")
+    d_tok = torch.empty((1, w.steps), dtype=torch.int32, device=f"cuda:{local}")
+    d_one = torch.empty((1, 1), dtype=torch.int32, device=f"cuda:{local}")
+
+    def call(n, out):
+        engine.generate_device(d_ctx.data_ptr(), 1, ctx.shape[1], n, out.data_ptr())
+
+    for _ in range(warmup):
+        call(w.steps, d_tok)
+        call(1, d_one)
+    torch.cuda.synchronize()
+
+    def timed(n, out, reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            call(n, out)
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+
+    full_ms = timed(w.steps, d_tok, steps)
+    prefill_ms = timed(1, d_one, steps)
+    per_token_ms = (full_ms - prefill_ms) / (w.steps - 1)
+    prof, kernels = profile_summary(engine, lambda: call(w.steps, d_tok))
+    hbm, _, src = measured_peaks()
+    gemv = prof.get("gemv")
+    gemv_gbs = gemv["bytes"] / (gemv["ms"] / 1000.0) / 1e9 if gemv and gemv["ms"] else None
+    attn = prof.get("attn_decode")
+    attn_gbs = attn["bytes"] / (attn["ms"] / 1000.0) / 1e9 if attn and attn["ms"] else None
+    engine.close()
+    return {"workload": w.name, "tokens_per_s": w.steps / (full_ms / 1000.0),
+            "ms_per_call": full_ms, "prefill_ms": prefill_ms,
+            "decode_ms_per_token": per_token_ms,
+            "gemv_GBps": gemv_gbs, "gemv_frac": gemv_gbs / hbm if gemv_gbs else None,
+            "attn_decode_GBps": attn_gbs, "peak_source": src, "kernels": kernels}
 
 
 def run_reference(args, rank, world):
@@ -298,12 +373,7 @@ def main():
     decode_tps = R * (steps - 1) / max(1e-9, (step_ms - prefill_ms) / 1000.0)
 
     # Per-kernel device time with CUDA events around each launch (one instrumented step).
-    engine.profile(True)
-    engine.profile_reset()
-    device_step()
-    torch.cuda.synchronize()
-    prof = engine.profile_read()
-    engine.profile(False)
+    prof, kernels = profile_summary(engine, device_step)
     top = max(prof.items(), key=lambda kv: kv[1]["ms"])
     name, k = top
     hbm, bf16, peak_src = measured_peaks()
@@ -318,12 +388,6 @@ def main():
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                     "frac": achieved / hbm, "traffic": None, "kernel": name,
                     "peak_source": peak_src}
-    total_ms = sum(v["ms"] for v in prof.values())
-    kernels = {n: {"launches": v["launches"], "ms": round(v["ms"], 3),
-                   "share": round(v["ms"] / total_ms, 4),
-                   "GB/s": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1) if v["ms"] else None,
-                   "TFLOP/s": round(v["flops"] / (v["ms"] / 1000.0) / 1e12, 2) if v["ms"] else None}
-               for n, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
 
     line = {
         "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -346,6 +410,8 @@ def main():
         "kernels": kernels,
         "clocks": clocks.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_batch1:
+        line["batch1"] = batch1(local, max(1, args.steps), max(1, args.warmup))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(workload, wpath)
     if dist:
