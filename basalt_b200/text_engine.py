@@ -289,6 +289,11 @@ class TextEngine:
         self._call(self._lib.bst_get_rng_state(self._h, ctypes.byref(v)))
         return v.value
 
+    @rng_state.setter
+    def rng_state(self, state: int):
+        """Sets the raw 48-bit java.util.Random state (see basalt_b200.sharding)."""
+        self._call(self._lib.bst_set_rng_state(self._h, int(state)))
+
     # ---- weights (TextEngine.java:298-350, Module.java:59-76) ----
     def save(self, path):
         if path is None:

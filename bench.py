@@ -284,11 +284,18 @@ def main():
     engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
     engine.load(wpath)
 
-    # This rank's shard of the prompts (rows rank*R .. rank*R + R of one seeded draw).
-    R = workload.rows
-    prompts = synthetic_prompts(workload.prompt_seed, R * world, workload.prompt, m.vocabulary)
-    ctx = left_pad(prompts[rank * R:(rank + 1) * R], m.window, m.vocabulary)
+    # This rank's contiguous shard of one seeded draw of rows x world prompts (weak scaling:
+    # `rows` per GPU). Sampling workloads start the shard's generator where the unsharded run
+    # would be at its first row.
+    from basalt_b200.sharding import shard_rng_state, shard_rows
+
+    first, R = shard_rows(workload.rows * world, world, rank)
+    prompts = synthetic_prompts(workload.prompt_seed, workload.rows * world, workload.prompt,
+                                m.vocabulary)
+    ctx = left_pad(prompts[first:first + R], m.window, m.vocabulary)
     steps = workload.steps
+    if workload.mode == "sample":
+        engine.rng_state = shard_rng_state(workload.sample_seed, steps, first)
 
     stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
     d_ctx = torch.from_numpy(ctx).to(f"cuda:{local}")

@@ -1,0 +1,84 @@
+"""Other model families and engine modes against the oracle: Zoo.charLm (zoo/Zoo.java:135-168),
+the bf16 KV cache, and decoding in waves (max_rows) with per-row generator states."""
+import numpy as np
+import pytest
+
+from basalt_b200 import ModelSpec, TextEngine, left_pad, synthetic_prompts, write_synthetic_weights
+from oracle import oracle as orc
+from parity import Report, check_greedy_row, check_sampled_row, compare_logits, top2_gap
+
+pytestmark = pytest.mark.gpu
+
+
+def pair(runtime, spec, path, seed=0, stddev=0.02):
+    write_synthetic_weights(spec, path, seed, stddev)
+    engine = TextEngine.of(runtime, spec, spec.vocabulary, spec.window)
+    engine.load(path)
+    family = {"padded_decoder": orc.FAMILY_PADDED_DECODER, "decoder": orc.FAMILY_DECODER,
+              "char_lm": orc.FAMILY_CHAR_LM}[spec.family]
+    oracle = orc.OracleEngine(family, spec.vocabulary, spec.window, spec.dimension, spec.layers,
+                              spec.heads, spec.hidden)
+    oracle.load(path)
+    return engine, oracle
+
+
+@pytest.mark.parametrize("rows", [1, 6, 12])
+def test_char_lm_decode_matches_the_oracle(runtime, tmp_path, rows):
+    # Zoo.charLm(engine, vocabulary 30, window 8, dimension 16, hidden 64): flat width 128.
+    # 1 and 6 rows take the GEMV path, 12 rows the tensor-core path.
+    spec = ModelSpec("char_lm", 30, 8, 16, hidden=64)
+    engine, oracle = pair(runtime, spec, tmp_path / "w.bin", seed=3, stddev=0.3)
+    ctx = synthetic_prompts(21, rows, 11, 30)
+    tokens, logits = engine.generateWithLogits(ctx, 20)
+    report = Report()
+    for r in range(rows):
+        check_greedy_row(oracle, ctx[r], tokens[r], logits[r], report, f"row{r}")
+    assert not report.mismatches, report.mismatches[:3]
+    assert len(report.near_ties) <= 1
+    np.testing.assert_array_equal(oracle.generate(ctx[0], 20), tokens[0])
+
+
+def test_char_lm_rejects_ids_outside_the_vocabulary(runtime, tmp_path):
+    from basalt_b200 import IllegalArgumentException
+
+    spec = ModelSpec("char_lm", 30, 4, 8, hidden=16)
+    engine, _ = pair(runtime, spec, tmp_path / "w.bin")
+    with pytest.raises(IllegalArgumentException, match="outside"):
+        engine.generate([1, 2, 3, 30], 1)
+
+
+def test_bf16_kv_cache_holds_a_stated_tolerance(runtime, tmp_path):
+    # KV stored in bf16 (8 mantissa bits) against the fp32 oracle: logits within 2e-2, tokens
+    # identical except where the oracle's top-2 gap is below that tolerance.
+    tol = 2e-2
+    spec = ModelSpec("padded_decoder", 512, 96, 256, 3, 4, 768, kv_dtype="bf16")
+    engine, oracle = pair(runtime, spec, tmp_path / "w.bin")
+    ctx = left_pad(synthetic_prompts(8, 4, 40, 512), 96, 512)
+    tokens, logits = engine.generateWithLogits(ctx, 40)
+    mismatched = 0
+    for r in range(4):
+        ref = oracle.forced_scores(ctx[r], tokens[r])
+        compare_logits(logits[r], ref, atol=tol, rtol=0, where=f"row{r}")
+        for step in range(40):
+            if int(np.argmax(ref[step])) != tokens[r, step]:
+                assert top2_gap(ref[step]) < tol
+                mismatched += 1
+    assert mismatched <= 4
+
+
+def test_waves_sample_exactly_like_one_batch(runtime, tmp_path):
+    # max_rows = 3 decodes 8 rows in three waves; every row keeps its own generator state, so the
+    # result equals 8 successive streamSampled calls on one seeded engine.
+    spec = ModelSpec("padded_decoder", 64, 32, 64, 2, 2, 128, max_rows=3)
+    engine, oracle = pair(runtime, spec, tmp_path / "w.bin", seed=4, stddev=0.1)
+    ctx = left_pad(synthetic_prompts(6, 8, 12, 64), 32, 64)
+    engine.seed(13)
+    tokens, logits = engine.sampleWithLogits(ctx, 15, 1.3, 10)
+    start = orc.lcg_scramble(13)
+    assert engine.rng_state == orc.lcg_advance(start, 2 * 15 * 8)
+    report = Report()
+    for r in range(8):
+        state = orc.lcg_advance(start, 2 * 15 * r)
+        check_sampled_row(oracle, ctx[r], tokens[r], logits[r], 1.3, 10, state, report, f"row{r}")
+    assert not report.mismatches, report.mismatches[:3]
+    assert len(report.near_ties) <= 1
