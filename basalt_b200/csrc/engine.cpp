@@ -308,6 +308,7 @@ struct Workspace {
     int *tok_id = nullptr, *tok_pos = nullptr, *tok_row = nullptr;
     float *x = nullptr, *h = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr;
     float *last = nullptr, *last_h = nullptr, *logits = nullptr, *part = nullptr;
+    int* attn_tickets = nullptr;  // decode-attention split merge tickets [rows * heads]
     float *flat = nullptr, *mixed = nullptr;  // charLm
     float* history = nullptr;                 // per-step logits, when requested
     bool has_history = false;
@@ -464,7 +465,7 @@ class Engine {
     void plan(const std::vector<int32_t>& windows, int rows, int steps,
               std::vector<StepPlan>* plans, int* max_slots, int* max_tokens) const;
     int linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N, int K,
-               Epi epi, const EpiArgs& ea, const char* what);
+               Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln = nullptr);
     int enqueue_prefill(const StepPlan& p, size_t begin, size_t end);
     int enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens);
     int enqueue_direct(int rows);
@@ -747,6 +748,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
         add(reinterpret_cast<void**>(&ws.last_h), sizeof(float) * static_cast<size_t>(rows) * d);
         add(reinterpret_cast<void**>(&ws.part),
             sizeof(float) * static_cast<size_t>(rows) * H * splits * (hd + 2));
+        add(reinterpret_cast<void**>(&ws.attn_tickets), sizeof(int) * static_cast<size_t>(rows) * H);
         ws.kv_layer_elems = static_cast<size_t>(rows) * H * slots * hd;
         const size_t kvb = (kvbf16 ? 2 : 4) * ws.kv_layer_elems * L;
         add(&ws.k_cache, kvb);
@@ -779,6 +781,10 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     ws.has_history = history;
     ws.generation = next_generation++;
     err = bst::launch_iota(stream, ws.rowmap_all, rows);
+    if (!err && ws.attn_tickets) {
+        err = cudaMemsetAsync(ws.attn_tickets, 0, sizeof(int) * static_cast<size_t>(rows) * H,
+                              stream);
+    }
     if (err != cudaSuccess) return cuda_fail(err, "initialising the workspace");
     return BST_OK;
 }
@@ -838,14 +844,24 @@ void Engine::plan(const std::vector<int32_t>& windows, int rows, int steps,
 // One projection: GEMV (M <= 8) or tiled FFMA for odd shapes, otherwise split the operand and
 // run the tcgen05 GEMM.
 int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N,
-                   int K, Epi epi, const EpiArgs& ea, const char* what) {
+                   int K, Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln) {
     const double wb = wbf16 ? 2.0 : 4.0;
     cudaError_t err;
     if (bst::tc_usable(M, N, K, wbf16) && (wbf16 || m.hi)) {
+        // Tensor-core path: the operand is split into hi/lo planes, by the LayerNorm when one
+        // precedes the projection, otherwise by a split pass.
         const double plane = static_cast<double>(bst::tc_split_bytes(M, K, wbf16));
-        err = launch(bst::kSplit, M * K * 4.0 + 2 * plane, 0, 1, [&] {
-            return bst::launch_split_operand(stream, x, ldx, M, K, wbf16, ws.xs_hi, ws.xs_lo);
-        });
+        const int planes = wbf16 ? 2 : 1;
+        if (ln) {
+            err = launch(bst::kLayerNorm, M * K * 4.0 + 2 * plane, 0, 1, [&] {
+                return bst::launch_layernorm(stream, x, ldx, ln->gamma, ln->beta, nullptr, 0, M,
+                                             K, ln->eps, ws.xs_hi, ws.xs_lo, planes);
+            });
+        } else {
+            err = launch(bst::kSplit, M * K * 4.0 + 2 * plane, 0, 1, [&] {
+                return bst::launch_split_operand(stream, x, ldx, M, K, wbf16, ws.xs_hi, ws.xs_lo);
+            });
+        }
         if (err) return cuda_fail(err, what);
         const double wbytes = static_cast<double>(N) * K * (wbf16 ? 2.0 : 8.0);
         // A split-K GEMM is two kernels (partial products, then the ordered fix-up).
@@ -860,11 +876,26 @@ int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, 
                      });
         return err ? cuda_fail(err, what) : BST_OK;
     }
+    const bst::LnArgs* fused = nullptr;
+    if (ln) {
+        if (bst::linear_fuses_layernorm(M, N, K)) {
+            fused = ln;  // the GEMV normalises its input rows itself
+        } else {
+            err = launch(bst::kLayerNorm, M * K * 8.0, 0, 1, [&] {
+                return bst::launch_layernorm(stream, x, ldx, ln->gamma, ln->beta, ws.h, K, M, K,
+                                             ln->eps);
+            });
+            if (err) return cuda_fail(err, what);
+            x = ws.h;
+            ldx = K;
+        }
+    }
     const int cls = bst::linear_uses_gemv(M, N, K) ? bst::kGemv : bst::kMisc;
     err = launch(cls, static_cast<double>(N) * K * wb + static_cast<double>(M) * K * 4 +
                           static_cast<double>(M) * N * 4,
                  2.0 * M * N * K, 1, [&] {
-                     return bst::launch_linear(stream, x, ldx, m.w, wbf16, bias, M, N, K, epi, ea);
+                     return bst::launch_linear(stream, x, ldx, m.w, wbf16, bias, M, N, K, epi, ea,
+                                               fused);
                  });
     return err ? cuda_fail(err, what) : BST_OK;
 }
@@ -916,11 +947,7 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
     }
     for (int l = 0; l < L; ++l) {
         const LayerWeights& lw = layers[l];
-        st = check(launch(bst::kLayerNorm, T * d * 8.0, 0, 1, [&] {
-                       return bst::launch_layernorm(stream, ws.x, d, lw.ln1_g, lw.ln1_b, ws.h, d, T, d,
-                                                    kLayerNormEps);
-                   }), "layernorm");
-        if (st) return st;
+        const bst::LnArgs ln1{lw.ln1_g, lw.ln1_b, kLayerNormEps};
         EpiArgs qkv;
         qkv.out = ws.q;
         qkv.ldo = d;
@@ -933,7 +960,7 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         qkv.head_dim = hd;
         qkv.slots = slots;
         qkv.kv_bf16 = kvbf16;
-        st = linear(ws.h, d, lw.wqkv, lw.bqkv, T, 3 * d, d, Epi::kQkv, qkv, "qkv projection");
+        st = linear(ws.x, d, lw.wqkv, lw.bqkv, T, 3 * d, d, Epi::kQkv, qkv, "qkv projection", &ln1);
         if (st) return st;
         st = check(launch(bst::kAttnPrefill, attn_bytes, attn_flops, 1, [&] {
                        return bst::launch_attn_prefill(stream, ws.q, qkv.k_cache, qkv.v_cache,
@@ -947,15 +974,11 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         res.ldo = d;
         st = linear(ws.att, d, lw.wo, lw.bo, T, d, d, Epi::kResidual, res, "output projection");
         if (st) return st;
-        st = check(launch(bst::kLayerNorm, T * d * 8.0, 0, 1, [&] {
-                       return bst::launch_layernorm(stream, ws.x, d, lw.ln2_g, lw.ln2_b, ws.h, d, T, d,
-                                                    kLayerNormEps);
-                   }), "layernorm");
-        if (st) return st;
+        const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
-        st = linear(ws.h, d, lw.w1, lw.b1, T, F, d, Epi::kGelu, act, "ffn1");
+        st = linear(ws.x, d, lw.w1, lw.b1, T, F, d, Epi::kGelu, act, "ffn1", &ln2);
         if (st) return st;
         st = linear(ws.ffn, F, lw.w2, lw.b2, T, d, F, Epi::kResidual, res, "ffn2");
         if (st) return st;
@@ -965,16 +988,12 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
                                                   ws.last);
                }), "gather last");
     if (st) return st;
-    st = check(launch(bst::kLayerNorm, segs * d * 8.0, 0, 1, [&] {
-                   return bst::launch_layernorm(stream, ws.last, d, lnf_g, lnf_b, ws.last_h, d,
-                                                segs, d, kLayerNormEps);
-               }), "final layernorm");
-    if (st) return st;
+    const bst::LnArgs lnf{lnf_g, lnf_b, kLayerNormEps};
     EpiArgs lg;
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = ws.seg_row;
-    return linear(ws.last_h, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head");
+    return linear(ws.last, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head", &lnf);
 }
 
 int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens) {
@@ -1001,11 +1020,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     if (st) return st;
     for (int l = 0; l < L; ++l) {
         const LayerWeights& lw = layers[l];
-        st = check(launch(bst::kLayerNorm, R * d * 8.0, 0, 1, [&] {
-                       return bst::launch_layernorm(stream, ws.x, d, lw.ln1_g, lw.ln1_b, ws.h, d, R, d,
-                                                    kLayerNormEps);
-                   }), "layernorm");
-        if (st) return st;
+        const bst::LnArgs ln1{lw.ln1_g, lw.ln1_b, kLayerNormEps};
         EpiArgs qkv;
         qkv.out = ws.q;
         qkv.ldo = d;
@@ -1018,47 +1033,36 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         qkv.head_dim = hd;
         qkv.slots = slots;
         qkv.kv_bf16 = kvbf16;
-        st = linear(ws.h, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv, "qkv projection");
+        st = linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv, "qkv projection", &ln1);
         if (st) return st;
         const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0;
         st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * sum_len * d, 1, [&] {
                        return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
                                                       kvbf16, rowmap, ws.len, R, H, hd, slots,
-                                                      scale, splits, chunk, ws.part);
+                                                      scale, splits, chunk, ws.part,
+                                                      ws.attn_tickets, ws.att);
                    }), "decode attention");
-        if (st) return st;
-        st = check(launch(bst::kAttnCombine, R * H * splits * (hd + 2) * 4.0 + R * d * 4.0, 0, 1, [&] {
-                       return bst::launch_attn_combine(stream, ws.part, R, H, hd, splits, ws.att);
-                   }), "attention combine");
         if (st) return st;
         EpiArgs res;
         res.out = ws.x;
         res.ldo = d;
         st = linear(ws.att, d, lw.wo, lw.bo, R, d, d, Epi::kResidual, res, "output projection");
         if (st) return st;
-        st = check(launch(bst::kLayerNorm, R * d * 8.0, 0, 1, [&] {
-                       return bst::launch_layernorm(stream, ws.x, d, lw.ln2_g, lw.ln2_b, ws.h, d, R, d,
-                                                    kLayerNormEps);
-                   }), "layernorm");
-        if (st) return st;
+        const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
-        st = linear(ws.h, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1");
+        st = linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1", &ln2);
         if (st) return st;
         st = linear(ws.ffn, F, lw.w2, lw.b2, R, d, F, Epi::kResidual, res, "ffn2");
         if (st) return st;
     }
-    st = check(launch(bst::kLayerNorm, R * d * 8.0, 0, 1, [&] {
-                   return bst::launch_layernorm(stream, ws.x, d, lnf_g, lnf_b, ws.h, d, R, d,
-                                                kLayerNormEps);
-               }), "final layernorm");
-    if (st) return st;
+    const bst::LnArgs lnf{lnf_g, lnf_b, kLayerNormEps};
     EpiArgs lg;
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = rowmap;
-    return linear(ws.h, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head");
+    return linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head", &lnf);
 }
 
 // Families without a cache: the whole window is the input every step.

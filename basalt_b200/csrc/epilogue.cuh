@@ -16,6 +16,20 @@ __device__ __forceinline__ float gelu_ref(float v) {
     return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
 }
 
+// Stores v as the tensor-core operand split at element idx: planes = 1 writes the tf32 truncation
+// and the fp32 remainder, planes = 2 two bf16 values (hi, and the rounded remainder).
+__device__ __forceinline__ void store_split(float v, int planes, void* hi, void* lo, size_t idx) {
+    if (planes == 1) {
+        const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        static_cast<float*>(hi)[idx] = h;
+        static_cast<float*>(lo)[idx] = __fsub_rn(v, h);
+    } else {
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        static_cast<__nv_bfloat16*>(hi)[idx] = h;
+        static_cast<__nv_bfloat16*>(lo)[idx] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+    }
+}
+
 template <Epi E>
 __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float v) {
     if constexpr (E == Epi::kStore) {

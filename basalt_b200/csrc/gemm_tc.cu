@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "device.cuh"
 #include "epilogue.cuh"
 #include "kernels.h"
 
@@ -197,6 +198,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // Set-up above touches no data of earlier kernels; operands and outputs only after the wait.
+    pdl_trigger();
+    pdl_wait();
 
     auto stage_a = [&](int s, int p) { return base + s * C::kStageBytes + p * C::kBytesA; };
     auto stage_b = [&](int s, int p) {
@@ -307,6 +311,8 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
 template <Epi E>
 __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int M, int N,
                                 const float* __restrict__ bias, EpiArgs ea) {
+    pdl_trigger();
+    pdl_wait();
     const size_t total = static_cast<size_t>(M) * N;
     for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
          e += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -320,6 +326,8 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int 
 // Operand split: hi/lo planes of X (see the file comment).
 __global__ void k_split_tf32(const float* __restrict__ x, int ldx, int M, int K,
                              float* __restrict__ hi, float* __restrict__ lo) {
+    pdl_trigger();
+    pdl_wait();
     const size_t total = static_cast<size_t>(M) * K;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -333,6 +341,8 @@ __global__ void k_split_tf32(const float* __restrict__ x, int ldx, int M, int K,
 
 __global__ void k_split_bf16(const float* __restrict__ x, int ldx, int M, int K,
                              __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    pdl_trigger();
+    pdl_wait();
     const size_t total = static_cast<size_t>(M) * K;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -388,14 +398,13 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
                          int N, int K, const EpiArgs& ea, int* err, const SplitK& sk) {
     using C = Config<FMT, BN>;
     const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits);
-    k_gemm_tc<FMT, BN, E><<<grid, kThreads, C::kSmem, s>>>(a0, a1, b0, b1, bias, M, N, K, ea, err,
-                                                           sk.splits, sk.part);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_gemm_tc<FMT, BN, E>, grid, dim3(kThreads), C::kSmem, s, a0, a1, b0,
+                               b1, bias, M, N, K, ea, err, sk.splits, sk.part);
     if (e != cudaSuccess || sk.splits == 1) return e;
     const size_t total = static_cast<size_t>(M) * N;
     const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
-    k_splitk_reduce<E><<<blocks, 256, 0, s>>>(sk.part, sk.splits, M, N, bias, ea);
-    return cudaGetLastError();
+    return launch_pdl(k_splitk_reduce<E>, dim3(blocks), dim3(256), 0, s, sk.part, sk.splits, M, N,
+                      bias, ea);
 }
 
 template <int FMT, int BN>
@@ -461,13 +470,11 @@ cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M,
     const size_t total = static_cast<size_t>(M) * K;
     const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 16));
     if (w_bf16) {
-        k_split_bf16<<<blocks, 256, 0, s>>>(x, ldx, M, K, static_cast<__nv_bfloat16*>(hi),
-                                            static_cast<__nv_bfloat16*>(lo));
-    } else {
-        k_split_tf32<<<blocks, 256, 0, s>>>(x, ldx, M, K, static_cast<float*>(hi),
-                                            static_cast<float*>(lo));
+        return launch_pdl(k_split_bf16, dim3(blocks), dim3(256), 0, s, x, ldx, M, K,
+                          static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
     }
-    return cudaGetLastError();
+    return launch_pdl(k_split_tf32, dim3(blocks), dim3(256), 0, s, x, ldx, M, K,
+                      static_cast<float*>(hi), static_cast<float*>(lo));
 }
 
 int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out) {

@@ -11,6 +11,7 @@
 // reference does). Nothing here traps: invalid ids are rejected on the host before launch.
 
 #include "kernels.h"
+#include "device.cuh"
 #include "epilogue.cuh"
 
 #include <cuda_bf16.h>
@@ -88,56 +89,154 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // with up to MT activation rows. KS warps split one column's K range; 8 / KS columns per CTA.
 // Weight rows stream from HBM once with 16-byte coalesced loads; activations hit L1.
 // ---------------------------------------------------------------------------------------------
+// Block-level LayerNorm of `rows` rows of x into out ([rows][d], shared memory), with the
+// statistics of nn_ops.rs:168-199 (f64 mean and population variance, f32 affine). One row uses
+// all eight warps; several rows take one warp each.
+__device__ void layernorm_rows(const float* __restrict__ x, int ldx, int rows, int d,
+                               const LnArgs& ln, float* __restrict__ out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ double red[8];
+    __shared__ double s_stat[2];
+    if (rows == 1) {
+        double s = 0.0;
+        for (int k = threadIdx.x; k < d; k += blockDim.x) s = __dadd_rn(s, static_cast<double>(x[k]));
+        s = warp_sum_d(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int w2 = 0; w2 < static_cast<int>(blockDim.x >> 5); ++w2) t = __dadd_rn(t, red[w2]);
+            s_stat[0] = __ddiv_rn(t, static_cast<double>(d));
+        }
+        __syncthreads();
+        const double mean = s_stat[0];
+        double v = 0.0;
+        for (int k = threadIdx.x; k < d; k += blockDim.x) {
+            const double delta = __dadd_rn(static_cast<double>(x[k]), -mean);
+            v = __dadd_rn(v, __dmul_rn(delta, delta));
+        }
+        v = warp_sum_d(v);
+        __syncthreads();
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int w2 = 0; w2 < static_cast<int>(blockDim.x >> 5); ++w2) t = __dadd_rn(t, red[w2]);
+            const double variance = __ddiv_rn(t, static_cast<double>(d));
+            s_stat[1] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(ln.eps))));
+        }
+        __syncthreads();
+        const double inverse = s_stat[1];
+        for (int k = threadIdx.x; k < d; k += blockDim.x) {
+            const float nrm = static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(x[k]), -mean), inverse));
+            out[k] = __fadd_rn(__fmul_rn(nrm, ln.gamma[k]), ln.beta[k]);
+        }
+        return;
+    }
+    if (warp >= rows) return;
+    const float* xr = x + static_cast<size_t>(warp) * ldx;
+    float* yr = out + static_cast<size_t>(warp) * d;
+    double s = 0.0;
+    for (int k = lane; k < d; k += 32) s = __dadd_rn(s, static_cast<double>(xr[k]));
+    const double mean = __ddiv_rn(warp_sum_d(s), static_cast<double>(d));
+    double v = 0.0;
+    for (int k = lane; k < d; k += 32) {
+        const double delta = __dadd_rn(static_cast<double>(xr[k]), -mean);
+        v = __dadd_rn(v, __dmul_rn(delta, delta));
+    }
+    const double variance = __ddiv_rn(warp_sum_d(v), static_cast<double>(d));
+    const double inverse = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(ln.eps))));
+    for (int k = lane; k < d; k += 32) {
+        const float nrm = static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(xr[k]), -mean), inverse));
+        yr[k] = __fadd_rn(__fmul_rn(nrm, ln.gamma[k]), ln.beta[k]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// GEMV for small M: each output column n is a dot product of W's row n (contiguous, K-major)
+// with up to MT activation rows. KS warps split one column's K range; 8 / KS columns per CTA.
+// Weights are constant, so each lane loads its first NV 16-byte weight vectors before waiting on
+// the kernel that produces the activations: under programmatic dependent launch the weight
+// stream of this projection overlaps the previous kernel. With ln.gamma set, the CTA first
+// applies LayerNorm to its input rows (the pre-norm of TransformerBlock) in shared memory.
+// ---------------------------------------------------------------------------------------------
 template <typename WT, int MT, int KS, Epi E>
 __global__ __launch_bounds__(256) void k_gemv(const float* __restrict__ x, int ldx,
                                               const WT* __restrict__ w,
                                               const float* __restrict__ bias, int M, int N,
-                                              int K, EpiArgs ea) {
+                                              int K, LnArgs ln, EpiArgs ea) {
     constexpr int VEC = Vec16<WT>::N;
     constexpr int COLS = 8 / KS;
+    constexpr int NV = 4;
+    extern __shared__ float xs[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int col = warp / KS, part = warp % KS;
     const int n = blockIdx.x * COLS + col;
     const int m0 = blockIdx.y * MT;
     const int mcount = min(MT, M - m0);
+    const bool vector_path = (K % VEC) == 0 && (ln.gamma != nullptr || (ldx % 4) == 0);
+    const int nvec = K / VEC;
+    const int per = (nvec + KS - 1) / KS;
+    const int v0 = part * per, v1 = min(nvec, v0 + per);
+    const WT* wr = w + static_cast<size_t>(min(n, N - 1)) * K;
+    float wv[NV][VEC];
+    if (vector_path && n < N) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int v = v0 + lane + 32 * j;
+            if (v < v1) Vec16<WT>::load(wr + static_cast<size_t>(v) * VEC, wv[j]);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
+    const float* xr = x + static_cast<size_t>(m0) * ldx;
+    int ld = ldx;
+    if (ln.gamma != nullptr) {
+        layernorm_rows(xr, ldx, mcount, K, ln, xs);
+        __syncthreads();
+        xr = xs;
+        ld = K;
+    }
     float acc[MT];
 #pragma unroll
     for (int i = 0; i < MT; ++i) acc[i] = 0.0f;
-    if (n < N) {
-        const WT* wr = w + static_cast<size_t>(n) * K;
-        const float* xr = x + static_cast<size_t>(m0) * ldx;
-        if ((K % VEC) == 0 && (ldx % 4) == 0) {
-            const int nvec = K / VEC;
-            const int per = (nvec + KS - 1) / KS;
-            const int v0 = part * per, v1 = min(nvec, v0 + per);
-#pragma unroll 4
-            for (int v = v0 + lane; v < v1; v += 32) {
-                float wv[VEC];
-                Vec16<WT>::load(wr + static_cast<size_t>(v) * VEC, wv);
-                const int k = v * VEC;
+    auto fma_vec = [&](const float* wvec, int k) {
 #pragma unroll
-                for (int i = 0; i < MT; ++i) {
-                    if (i < mcount) {
-                        const float* xp = xr + static_cast<size_t>(i) * ldx + k;
+        for (int i = 0; i < MT; ++i) {
+            if (i < mcount) {
+                const float* xp = xr + static_cast<size_t>(i) * ld + k;
 #pragma unroll
-                        for (int c = 0; c < VEC; c += 4) {
-                            const float4 xv = *reinterpret_cast<const float4*>(xp + c);
-                            acc[i] = fmaf(wv[c], xv.x, acc[i]);
-                            acc[i] = fmaf(wv[c + 1], xv.y, acc[i]);
-                            acc[i] = fmaf(wv[c + 2], xv.z, acc[i]);
-                            acc[i] = fmaf(wv[c + 3], xv.w, acc[i]);
-                        }
-                    }
+                for (int c = 0; c < VEC; c += 4) {
+                    const float4 xv = *reinterpret_cast<const float4*>(xp + c);
+                    acc[i] = fmaf(wvec[c], xv.x, acc[i]);
+                    acc[i] = fmaf(wvec[c + 1], xv.y, acc[i]);
+                    acc[i] = fmaf(wvec[c + 2], xv.z, acc[i]);
+                    acc[i] = fmaf(wvec[c + 3], xv.w, acc[i]);
                 }
             }
+        }
+    };
+    if (n < N) {
+        if (vector_path) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const int v = v0 + lane + 32 * j;
+                if (v < v1) fma_vec(wv[j], v * VEC);
+            }
+#pragma unroll 4
+            for (int v = v0 + lane + 32 * NV; v < v1; v += 32) {
+                float wt[VEC];
+                Vec16<WT>::load(wr + static_cast<size_t>(v) * VEC, wt);
+                fma_vec(wt, v * VEC);
+            }
         } else {
-            const int per = (K + KS - 1) / KS;
-            const int k0 = part * per, k1 = min(K, k0 + per);
+            const int kper = (K + KS - 1) / KS;
+            const int k0 = part * kper, k1 = min(K, k0 + kper);
             for (int k = k0 + lane; k < k1; k += 32) {
                 const float wk = to_f(wr[k]);
 #pragma unroll
                 for (int i = 0; i < MT; ++i) {
-                    if (i < mcount) acc[i] = fmaf(wk, xr[static_cast<size_t>(i) * ldx + k], acc[i]);
+                    if (i < mcount) acc[i] = fmaf(wk, xr[static_cast<size_t>(i) * ld + k], acc[i]);
                 }
             }
         }
@@ -151,10 +250,10 @@ __global__ __launch_bounds__(256) void k_gemv(const float* __restrict__ x, int l
     }
     __syncthreads();
     if (part == 0 && lane < mcount && n < N) {
-        float s = 0.0f;
+        float sum = 0.0f;
 #pragma unroll
-        for (int p = 0; p < KS; ++p) s += red[col * KS + p][lane];
-        const float v = bias ? __fadd_rn(s, bias[n]) : s;
+        for (int p = 0; p < KS; ++p) sum += red[col * KS + p][lane];
+        const float v = bias ? __fadd_rn(sum, bias[n]) : sum;
         epi_apply<E>(ea, m0 + lane, n, v);
     }
 }
@@ -169,6 +268,8 @@ __global__ __launch_bounds__(256) void k_gemm(const float* __restrict__ a, int l
                                               const WT* __restrict__ b,
                                               const float* __restrict__ bias, int M, int N,
                                               int K, EpiArgs ea) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int BM = 128, BN = 128, BK = 16, PAD = 4;
     __shared__ __align__(16) float As[2][BK][BM + PAD];
     __shared__ __align__(16) float Bs[2][BK][BN + PAD];
@@ -288,6 +389,8 @@ template <typename WT>
 __global__ void k_embed_tokens(const WT* __restrict__ tok, const WT* __restrict__ pos,
                                const int* __restrict__ ids, const int* __restrict__ positions,
                                float* __restrict__ x, int d) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x;
     const size_t id = static_cast<size_t>(ids[t]);
     const size_t p = static_cast<size_t>(positions[t]);
@@ -301,6 +404,8 @@ __global__ void k_embed_decode(const WT* __restrict__ tok, const WT* __restrict_
                                const int* __restrict__ rowmap, const int* __restrict__ next,
                                int* __restrict__ len, int* __restrict__ slot,
                                float* __restrict__ x, int d) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x;
     const int row = rowmap[i];
     __shared__ int s_slot;
@@ -321,6 +426,8 @@ __global__ void k_embed_decode(const WT* __restrict__ tok, const WT* __restrict_
 template <typename WT>
 __global__ void k_window_embed(const int* __restrict__ window, int W, const WT* __restrict__ emb,
                                int d, float* __restrict__ x) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     for (int idx = threadIdx.x; idx < W * d; idx += blockDim.x) {
         const int t = idx / d, e = idx - t * d;
@@ -331,6 +438,8 @@ __global__ void k_window_embed(const int* __restrict__ window, int W, const WT* 
 
 __global__ void k_last_token(const int* __restrict__ window, int W, const float* __restrict__ w,
                              const float* __restrict__ bias, int V, float* __restrict__ logits) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const int token = window[static_cast<size_t>(r) * W + W - 1];
     const int t = ((token % V) + V) % V;  // Math.floorMod
@@ -345,6 +454,8 @@ __global__ void k_prefill_tokens(const int* __restrict__ window, int W,
                                  const int* __restrict__ seg_start, const int* __restrict__ seg_len,
                                  int pad_id, int* __restrict__ ids, int* __restrict__ positions,
                                  int* __restrict__ tok_row, int* __restrict__ len) {
+    pdl_trigger();
+    pdl_wait();
     const int j = blockIdx.x;
     const int row = seg_row[j], npad = seg_npad[j], start = seg_start[j], n = seg_len[j];
     for (int t = threadIdx.x; t < n; t += blockDim.x) {
@@ -357,6 +468,8 @@ __global__ void k_prefill_tokens(const int* __restrict__ window, int W,
 
 __global__ void k_gather_last(const float* __restrict__ x, const int* __restrict__ seg_start,
                               const int* __restrict__ seg_len, int d, float* __restrict__ last) {
+    pdl_trigger();
+    pdl_wait();
     const int j = blockIdx.x;
     const size_t src = static_cast<size_t>(seg_start[j] + seg_len[j] - 1) * d;
     for (int e = threadIdx.x; e < d; e += blockDim.x) last[static_cast<size_t>(j) * d + e] = x[src + e];
@@ -370,12 +483,15 @@ __global__ __launch_bounds__(256) void k_layernorm(const float* __restrict__ x, 
                                                    const float* __restrict__ gamma,
                                                    const float* __restrict__ beta,
                                                    float* __restrict__ y, int ldy, int rows, int d,
-                                                   float eps) {
+                                                   float eps, void* __restrict__ hi,
+                                                   void* __restrict__ lo, int planes) {
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= rows) return;
     const float* xr = x + static_cast<size_t>(row) * ldx;
-    float* yr = y + static_cast<size_t>(row) * ldy;
+    float* yr = y ? y + static_cast<size_t>(row) * ldy : nullptr;
     double s = 0.0;
     for (int i = lane; i < d; i += 32) s = __dadd_rn(s, static_cast<double>(xr[i]));
     const double mean = __ddiv_rn(warp_sum_d(s), static_cast<double>(d));
@@ -389,7 +505,9 @@ __global__ __launch_bounds__(256) void k_layernorm(const float* __restrict__ x, 
     for (int i = lane; i < d; i += 32) {
         const float normalized =
             static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(xr[i]), -mean), inverse));
-        yr[i] = __fadd_rn(__fmul_rn(normalized, gamma[i]), beta[i]);
+        const float out = __fadd_rn(__fmul_rn(normalized, gamma[i]), beta[i]);
+        if (y) yr[i] = out;
+        if (planes) store_split(out, planes, hi, lo, static_cast<size_t>(row) * d + i);
     }
 }
 
@@ -402,34 +520,29 @@ template <typename KT, int HD>
 __global__ __launch_bounds__(128) void k_attn_decode(
     const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
     const int* __restrict__ rowmap, const int* __restrict__ len, int heads, int slots,
-    float scale, int splits, int chunk, float* __restrict__ part) {
+    float scale, int splits, int chunk, float* __restrict__ part, int* __restrict__ tickets,
+    float* __restrict__ out) {
     constexpr int EPV = Vec16<KT>::N;
     constexpr int LPK = HD / EPV;  // lanes per key
     constexpr int KPW = 32 / LPK;  // keys per warp step
     constexpr int DPL = HD / 32;   // output dims per lane
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x / heads, h = blockIdx.x % heads, sp = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row = rowmap[i];
     const int T = len[row];
     const int start = sp * chunk, end = min(T, start + chunk);
+    const int n = max(0, end - start);
     const int d = heads * HD;
     __shared__ float qs[HD];
     __shared__ float sc[kMaxChunk];
     __shared__ float red[4 * HD];
     __shared__ float stat[8];
-    float* out = part + (static_cast<size_t>(i * heads + h) * splits + sp) * (HD + 2);
-    if (start >= end) {
-        for (int e = tid; e < HD; e += 128) out[e] = 0.0f;
-        if (tid == 0) {
-            out[HD] = -INFINITY;
-            out[HD + 1] = 0.0f;
-        }
-        return;
-    }
+    __shared__ int s_last;
     for (int e = tid; e < HD; e += 128) qs[e] = q[static_cast<size_t>(i) * d + h * HD + e];
     __syncthreads();
     const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
-    const int n = end - start;
     const int sub = lane % LPK, kk = lane / LPK;
     for (int j0 = warp * KPW; j0 < n; j0 += 4 * KPW) {
         const int j = j0 + kk;
@@ -474,32 +587,42 @@ __global__ __launch_bounds__(128) void k_attn_decode(
 #pragma unroll
     for (int c = 0; c < DPL; ++c) red[warp * HD + lane * DPL + c] = o[c];
     __syncthreads();
-    for (int e = tid; e < HD; e += 128) out[e] = red[e] + red[HD + e] + red[2 * HD + e] + red[3 * HD + e];
-    if (tid == 0) {
-        out[HD] = mx;
-        out[HD + 1] = sum;
-    }
-}
-
-template <int HD>
-__global__ void k_attn_combine(const float* __restrict__ part, int splits, int heads,
-                               float* __restrict__ out) {
-    const int ih = blockIdx.x;
-    const int i = ih / heads, h = ih % heads;
-    const float* p = part + static_cast<size_t>(ih) * splits * (HD + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * (HD + 2) + HD]);
-    for (int e = threadIdx.x; e < HD; e += blockDim.x) {
-        float L = 0.0f, O = 0.0f;
-        for (int s = 0; s < splits; ++s) {
-            const float ms = p[s * (HD + 2) + HD];
-            if (ms == -INFINITY) continue;
-            const float wgt = expf(ms - M);
-            L = fmaf(p[s * (HD + 2) + HD + 1], wgt, L);
-            O = fmaf(p[s * (HD + 2) + e], wgt, O);
+    if (splits == 1) {
+        for (int e = tid; e < HD; e += 128) {
+            const float acc = red[e] + red[HD + e] + red[2 * HD + e] + red[3 * HD + e];
+            out[static_cast<size_t>(i) * d + h * HD + e] = acc / sum;
         }
-        out[static_cast<size_t>(i) * heads * HD + h * HD + e] = O / L;
+        return;
     }
+    // Several splits: publish this split's (output, max, sum); the last split of the head to
+    // finish merges all of them in split order and re-arms the ticket.
+    float* mine = part + (static_cast<size_t>(i * heads + h) * splits + sp) * (HD + 2);
+    for (int e = tid; e < HD; e += 128) mine[e] = red[e] + red[HD + e] + red[2 * HD + e] + red[3 * HD + e];
+    if (tid == 0) {
+        mine[HD] = n > 0 ? mx : -INFINITY;
+        mine[HD + 1] = n > 0 ? sum : 0.0f;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&tickets[i * heads + h], 1) == splits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* all = part + static_cast<size_t>(i * heads + h) * splits * (HD + 2);
+    float M = -INFINITY;
+    for (int z = 0; z < splits; ++z) M = fmaxf(M, __ldcg(all + z * (HD + 2) + HD));
+    for (int e = tid; e < HD; e += 128) {
+        float L = 0.0f, O = 0.0f;
+        for (int z = 0; z < splits; ++z) {
+            const float mz = __ldcg(all + z * (HD + 2) + HD);
+            if (mz == -INFINITY) continue;
+            const float wgt = expf(mz - M);
+            L = fmaf(__ldcg(all + z * (HD + 2) + HD + 1), wgt, L);
+            O = fmaf(__ldcg(all + z * (HD + 2) + e), wgt, O);
+        }
+        out[static_cast<size_t>(i) * d + h * HD + e] = O / L;
+    }
+    if (tid == 0) tickets[i * heads + h] = 0;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -511,6 +634,8 @@ __global__ __launch_bounds__(128) void k_attn_prefill(
     const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
     const int* __restrict__ seg_row, const int* __restrict__ seg_start,
     const int* __restrict__ seg_len, int heads, int slots, float scale, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int QT = 4 * QPW;
     constexpr int DPL = HD / 32;
     const int j = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * QT;
@@ -627,6 +752,8 @@ __global__ __launch_bounds__(256) void k_select_greedy(const float* __restrict__
                                                        int W, int steps, int rows, int* step,
                                                        int* done, int* tokens, int* next,
                                                        int* window) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const float* lr = logits + static_cast<size_t>(r) * V;
     __shared__ int s_step;
@@ -703,6 +830,8 @@ __global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict_
                                                         double temperature, int top_k,
                                                         uint64_t* rng, int* step, int* done,
                                                         int* tokens, int* next, int* window) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem[];
     uint64_t* keys = reinterpret_cast<uint64_t*>(smem);
     int* order = reinterpret_cast<int*>(keys + P);
@@ -758,6 +887,8 @@ __global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict_
 
 __global__ void k_stash_logits(const float* __restrict__ logits, int V, int steps,
                                const int* __restrict__ step, float* __restrict__ history) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.y;
     const int g = *step;
     const int v = blockIdx.x * blockDim.x + threadIdx.x;
@@ -767,10 +898,14 @@ __global__ void k_stash_logits(const float* __restrict__ logits, int V, int step
 }
 
 __global__ void k_fill_int(int* p, int value, int count) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < count) p[i] = value;
 }
 __global__ void k_iota(int* p, int count) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < count) p[i] = i;
 }
@@ -791,42 +926,43 @@ int pick_ks(int columns, int row_groups, int nvec) {
 
 template <typename WT, int MT, Epi E>
 cudaError_t gemv_ks(cudaStream_t s, const float* x, int ldx, const void* w, const float* bias,
-                    int M, int N, int K, const EpiArgs& ea) {
+                    int M, int N, int K, const LnArgs& ln, const EpiArgs& ea) {
     const int row_groups = (M + MT - 1) / MT;
     const int ks = pick_ks(N, row_groups, K / Vec16<WT>::N);
     const WT* wt = static_cast<const WT*>(w);
     const dim3 block(256);
+    const size_t smem = ln.gamma ? static_cast<size_t>(MT) * K * sizeof(float) : 0;
     switch (ks) {
-        case 1: k_gemv<WT, MT, 1, E><<<dim3((N + 7) / 8, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
-        case 2: k_gemv<WT, MT, 2, E><<<dim3((N + 3) / 4, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
-        case 4: k_gemv<WT, MT, 4, E><<<dim3((N + 1) / 2, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
-        default: k_gemv<WT, MT, 8, E><<<dim3(N, row_groups), block, 0, s>>>(x, ldx, wt, bias, M, N, K, ea); break;
+        case 1: return launch_pdl(k_gemv<WT, MT, 1, E>, dim3((N + 7) / 8, row_groups), block, smem, s, x, ldx, wt, bias, M, N, K, ln, ea);
+        case 2: return launch_pdl(k_gemv<WT, MT, 2, E>, dim3((N + 3) / 4, row_groups), block, smem, s, x, ldx, wt, bias, M, N, K, ln, ea);
+        case 4: return launch_pdl(k_gemv<WT, MT, 4, E>, dim3((N + 1) / 2, row_groups), block, smem, s, x, ldx, wt, bias, M, N, K, ln, ea);
+        default: return launch_pdl(k_gemv<WT, MT, 8, E>, dim3(N, row_groups), block, smem, s, x, ldx, wt, bias, M, N, K, ln, ea);
     }
-    return cudaGetLastError();
 }
 
 template <typename WT, Epi E>
 cudaError_t linear_typed(cudaStream_t s, const float* x, int ldx, const void* w,
-                         const float* bias, int M, int N, int K, const EpiArgs& ea) {
+                         const float* bias, int M, int N, int K, const EpiArgs& ea,
+                         const LnArgs& ln) {
     if (linear_uses_gemv(M, N, K)) {
-        if (M == 1) return gemv_ks<WT, 1, E>(s, x, ldx, w, bias, M, N, K, ea);
-        return gemv_ks<WT, 8, E>(s, x, ldx, w, bias, M, N, K, ea);
+        if (M == 1) return gemv_ks<WT, 1, E>(s, x, ldx, w, bias, M, N, K, ln, ea);
+        return gemv_ks<WT, 8, E>(s, x, ldx, w, bias, M, N, K, ln, ea);
     }
+    if (ln.gamma) return cudaErrorInvalidValue;  // the tiled GEMM takes normalised inputs
     const dim3 grid((N + 127) / 128, (M + 127) / 128);
-    k_gemm<WT, E><<<grid, 256, 0, s>>>(x, ldx, static_cast<const WT*>(w), bias, M, N, K, ea);
-    return cudaGetLastError();
+    return launch_pdl(k_gemm<WT, E>, grid, 256, 0, s, x, ldx, static_cast<const WT*>(w), bias, M, N, K, ea);
 }
 
 template <typename WT>
 cudaError_t linear_epi(cudaStream_t s, const float* x, int ldx, const void* w, const float* bias,
-                       int M, int N, int K, Epi epi, const EpiArgs& ea) {
+                       int M, int N, int K, Epi epi, const EpiArgs& ea, const LnArgs& ln) {
     switch (epi) {
-        case Epi::kStore: return linear_typed<WT, Epi::kStore>(s, x, ldx, w, bias, M, N, K, ea);
-        case Epi::kGelu: return linear_typed<WT, Epi::kGelu>(s, x, ldx, w, bias, M, N, K, ea);
-        case Epi::kResidual: return linear_typed<WT, Epi::kResidual>(s, x, ldx, w, bias, M, N, K, ea);
-        case Epi::kResidualGelu: return linear_typed<WT, Epi::kResidualGelu>(s, x, ldx, w, bias, M, N, K, ea);
-        case Epi::kQkv: return linear_typed<WT, Epi::kQkv>(s, x, ldx, w, bias, M, N, K, ea);
-        case Epi::kLogits: return linear_typed<WT, Epi::kLogits>(s, x, ldx, w, bias, M, N, K, ea);
+        case Epi::kStore: return linear_typed<WT, Epi::kStore>(s, x, ldx, w, bias, M, N, K, ea, ln);
+        case Epi::kGelu: return linear_typed<WT, Epi::kGelu>(s, x, ldx, w, bias, M, N, K, ea, ln);
+        case Epi::kResidual: return linear_typed<WT, Epi::kResidual>(s, x, ldx, w, bias, M, N, K, ea, ln);
+        case Epi::kResidualGelu: return linear_typed<WT, Epi::kResidualGelu>(s, x, ldx, w, bias, M, N, K, ea, ln);
+        case Epi::kQkv: return linear_typed<WT, Epi::kQkv>(s, x, ldx, w, bias, M, N, K, ea, ln);
+        case Epi::kLogits: return linear_typed<WT, Epi::kLogits>(s, x, ldx, w, bias, M, N, K, ea, ln);
     }
     return cudaErrorInvalidValue;
 }
@@ -838,11 +974,20 @@ bool linear_uses_gemv(int M, int N, int K) {
     return M <= 8 || (K % 16) != 0;
 }
 
+bool linear_fuses_layernorm(int M, int N, int K) {
+    const int mt = M == 1 ? 1 : 8;
+    return linear_uses_gemv(M, N, K) && static_cast<size_t>(mt) * K * sizeof(float) <= 48 * 1024;
+}
+
 cudaError_t launch_linear(cudaStream_t s, const float* x, int ldx, const void* w, int w_bf16,
-                          const float* bias, int M, int N, int K, Epi epi, const EpiArgs& ea) {
+                          const float* bias, int M, int N, int K, Epi epi, const EpiArgs& ea,
+                          const LnArgs* ln) {
     if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-    return w_bf16 ? linear_epi<__nv_bfloat16>(s, x, ldx, w, bias, M, N, K, epi, ea)
-                  : linear_epi<float>(s, x, ldx, w, bias, M, N, K, epi, ea);
+    LnArgs none;
+    const LnArgs& use = ln ? *ln : none;
+    if (use.gamma && !linear_fuses_layernorm(M, N, K)) return cudaErrorInvalidValue;
+    return w_bf16 ? linear_epi<__nv_bfloat16>(s, x, ldx, w, bias, M, N, K, epi, ea, use)
+                  : linear_epi<float>(s, x, ldx, w, bias, M, N, K, epi, ea, use);
 }
 
 cudaError_t launch_embed_tokens(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
@@ -850,16 +995,17 @@ cudaError_t launch_embed_tokens(cudaStream_t s, const void* tok, const void* pos
                                 int d) {
     if (count <= 0) return cudaSuccess;
     const int threads = d >= 256 ? 256 : 128;
+    cudaError_t err;
     if (w_bf16) {
-        k_embed_tokens<__nv_bfloat16><<<count, threads, 0, s>>>(
+        err = launch_pdl(k_embed_tokens<__nv_bfloat16>, count, threads, 0, s, 
             static_cast<const __nv_bfloat16*>(tok), static_cast<const __nv_bfloat16*>(pos), ids,
             positions, x, d);
     } else {
-        k_embed_tokens<float><<<count, threads, 0, s>>>(static_cast<const float*>(tok),
+        err = launch_pdl(k_embed_tokens<float>, count, threads, 0, s, static_cast<const float*>(tok),
                                                         static_cast<const float*>(pos), ids,
                                                         positions, x, d);
     }
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
@@ -867,34 +1013,36 @@ cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos
                                 int R, int d) {
     if (R <= 0) return cudaSuccess;
     const int threads = d >= 256 ? 256 : 128;
+    cudaError_t err;
     if (w_bf16) {
-        k_embed_decode<__nv_bfloat16><<<R, threads, 0, s>>>(
+        err = launch_pdl(k_embed_decode<__nv_bfloat16>, R, threads, 0, s, 
             static_cast<const __nv_bfloat16*>(tok), static_cast<const __nv_bfloat16*>(pos),
             rowmap, next, len, slot, x, d);
     } else {
-        k_embed_decode<float><<<R, threads, 0, s>>>(static_cast<const float*>(tok),
+        err = launch_pdl(k_embed_decode<float>, R, threads, 0, s, static_cast<const float*>(tok),
                                                     static_cast<const float*>(pos), rowmap, next,
                                                     len, slot, x, d);
     }
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const float* gamma,
-                             const float* beta, float* y, int ldy, int rows, int d, float eps) {
+                             const float* beta, float* y, int ldy, int rows, int d, float eps,
+                             void* hi, void* lo, int planes) {
     if (rows <= 0) return cudaSuccess;
-    k_layernorm<<<(rows + 7) / 8, 256, 0, s>>>(x, ldx, gamma, beta, y, ldy, rows, d, eps);
-    return cudaGetLastError();
+    return launch_pdl(k_layernorm, (rows + 7) / 8, 256, 0, s, x, ldx, gamma, beta, y, ldy, rows,
+                      d, eps, hi, lo, planes);
 }
 
 namespace {
 template <typename KT, int HD>
 cudaError_t attn_decode_typed(cudaStream_t s, const float* q, const void* kc, const void* vc,
                               const int* rowmap, const int* len, int R, int heads, int slots,
-                              float scale, int splits, int chunk, float* part) {
-    k_attn_decode<KT, HD><<<dim3(R * heads, splits), 128, 0, s>>>(
-        q, static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len, heads, slots,
-        scale, splits, chunk, part);
-    return cudaGetLastError();
+                              float scale, int splits, int chunk, float* part, int* tickets,
+                              float* out) {
+    return launch_pdl(k_attn_decode<KT, HD>, dim3(R * heads, splits), 128, 0, s, q,
+                      static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len, heads,
+                      slots, scale, splits, chunk, part, tickets, out);
 }
 
 template <typename KT, int HD>
@@ -904,22 +1052,21 @@ cudaError_t attn_prefill_typed(cudaStream_t s, const float* q, const void* kc, c
                                float* out) {
     constexpr int QPW = HD > 64 ? 4 : 8;
     const dim3 grid(segments, heads, (max_len + 4 * QPW - 1) / (4 * QPW));
-    k_attn_prefill<KT, HD, QPW><<<grid, 128, 0, s>>>(
+    return launch_pdl(k_attn_prefill<KT, HD, QPW>, grid, 128, 0, s, 
         q, static_cast<const KT*>(kc), static_cast<const KT*>(vc), seg_row, seg_start, seg_len,
         heads, slots, scale, out);
-    return cudaGetLastError();
 }
 }  // namespace
 
 cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
                                const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
                                int R, int heads, int head_dim, int slots, float scale, int splits,
-                               int chunk, float* part) {
+                               int chunk, float* part, int* tickets, float* out) {
     if (R <= 0) return cudaSuccess;
     if (chunk > kMaxChunk) return cudaErrorInvalidValue;
 #define BST_ATTN_DEC(KT, HD)                                                                    \
     return attn_decode_typed<KT, HD>(s, q, k_cache, v_cache, rowmap, len, R, heads, slots,      \
-                                     scale, splits, chunk, part)
+                                     scale, splits, chunk, part, tickets, out)
     if (kv_bf16) {
         switch (head_dim) {
             case 32: BST_ATTN_DEC(__nv_bfloat16, 32);
@@ -935,18 +1082,6 @@ cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cac
     }
 #undef BST_ATTN_DEC
     return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_attn_combine(cudaStream_t s, const float* part, int R, int heads, int head_dim,
-                                int splits, float* out) {
-    if (R <= 0) return cudaSuccess;
-    switch (head_dim) {
-        case 32: k_attn_combine<32><<<R * heads, 32, 0, s>>>(part, splits, heads, out); break;
-        case 64: k_attn_combine<64><<<R * heads, 64, 0, s>>>(part, splits, heads, out); break;
-        case 128: k_attn_combine<128><<<R * heads, 128, 0, s>>>(part, splits, heads, out); break;
-        default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,
@@ -980,36 +1115,34 @@ cudaError_t launch_prefill_tokens(cudaStream_t s, const int* window, int W, cons
                                   int segments, int pad_id, int* ids, int* positions, int* tok_row,
                                   int* len) {
     if (segments <= 0) return cudaSuccess;
-    k_prefill_tokens<<<segments, 256, 0, s>>>(window, W, seg_row, seg_npad, seg_start, seg_len,
+    return launch_pdl(k_prefill_tokens, segments, 256, 0, s, window, W, seg_row, seg_npad, seg_start, seg_len,
                                               pad_id, ids, positions, tok_row, len);
-    return cudaGetLastError();
 }
 
 cudaError_t launch_gather_last(cudaStream_t s, const float* x, const int* seg_start,
                                const int* seg_len, int segments, int d, float* last) {
     if (segments <= 0) return cudaSuccess;
-    k_gather_last<<<segments, 128, 0, s>>>(x, seg_start, seg_len, d, last);
-    return cudaGetLastError();
+    return launch_pdl(k_gather_last, segments, 128, 0, s, x, seg_start, seg_len, d, last);
 }
 
 cudaError_t launch_window_embed(cudaStream_t s, const int* window, int W, const void* emb,
                                 int w_bf16, int rows, int d, float* x) {
     if (rows <= 0) return cudaSuccess;
+    cudaError_t err;
     if (w_bf16) {
-        k_window_embed<__nv_bfloat16><<<rows, 256, 0, s>>>(
+        err = launch_pdl(k_window_embed<__nv_bfloat16>, rows, 256, 0, s, 
             window, W, static_cast<const __nv_bfloat16*>(emb), d, x);
     } else {
-        k_window_embed<float><<<rows, 256, 0, s>>>(window, W, static_cast<const float*>(emb), d,
+        err = launch_pdl(k_window_embed<float>, rows, 256, 0, s, window, W, static_cast<const float*>(emb), d,
                                                    x);
     }
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_last_token(cudaStream_t s, const int* window, int W, const float* weight,
                               const float* bias, int rows, int V, float* logits) {
     if (rows <= 0) return cudaSuccess;
-    k_last_token<<<rows, 128, 0, s>>>(window, W, weight, bias, V, logits);
-    return cudaGetLastError();
+    return launch_pdl(k_last_token, rows, 128, 0, s, window, W, weight, bias, V, logits);
 }
 
 cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, int V, int W,
@@ -1017,9 +1150,8 @@ cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, 
                                  int* window) {
     if (rows <= 0) return cudaSuccess;
     if (W > 8 * 256) return cudaErrorInvalidValue;
-    k_select_greedy<<<rows, 256, 0, s>>>(logits, V, W, steps, rows, step, done, tokens, next,
+    return launch_pdl(k_select_greedy, rows, 256, 0, s, logits, V, W, steps, rows, step, done, tokens, next,
                                          window);
-    return cudaGetLastError();
 }
 
 size_t select_sample_smem(int V) {
@@ -1037,10 +1169,9 @@ cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, 
     while (P < V) P <<= 1;
     const size_t smem = select_sample_smem(V);
     if (smem > kSampleSmemLimit) return cudaErrorInvalidValue;
-    k_select_sample<<<rows, 1024, smem, s>>>(logits, V, P, W, steps, rows,
+    return launch_pdl(k_select_sample, rows, 1024, smem, s, logits, V, P, W, steps, rows,
                                              static_cast<double>(temperature), top_k, rng, step,
                                              done, tokens, next, window);
-    return cudaGetLastError();
 }
 
 cudaError_t configure_device_kernels() {
@@ -1054,8 +1185,7 @@ cudaError_t configure_device_kernels() {
 cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,
                                 const int* step, float* history) {
     if (rows <= 0) return cudaSuccess;
-    k_stash_logits<<<dim3((V + 255) / 256, rows), 256, 0, s>>>(logits, V, steps, step, history);
-    return cudaGetLastError();
+    return launch_pdl(k_stash_logits, dim3((V + 255) / 256, rows), 256, 0, s, logits, V, steps, step, history);
 }
 
 cudaError_t configure_device_kernels_once(int device) {
@@ -1070,14 +1200,12 @@ cudaError_t configure_device_kernels_once(int device) {
 
 cudaError_t launch_fill_int(cudaStream_t s, int* p, int value, int count) {
     if (count <= 0) return cudaSuccess;
-    k_fill_int<<<(count + 255) / 256, 256, 0, s>>>(p, value, count);
-    return cudaGetLastError();
+    return launch_pdl(k_fill_int, (count + 255) / 256, 256, 0, s, p, value, count);
 }
 
 cudaError_t launch_iota(cudaStream_t s, int* p, int count) {
     if (count <= 0) return cudaSuccess;
-    k_iota<<<(count + 255) / 256, 256, 0, s>>>(p, count);
-    return cudaGetLastError();
+    return launch_pdl(k_iota, (count + 255) / 256, 256, 0, s, p, count);
 }
 
 }  // namespace bst

@@ -53,9 +53,20 @@ struct EpiArgs {
     int kv_bf16 = 0;
 };
 
+// Optional LayerNorm applied to a projection's input rows (the pre-norm of TransformerBlock).
+struct LnArgs {
+    const float* gamma = nullptr;
+    const float* beta = nullptr;
+    float eps = 0.0f;
+};
+
 // Y = X[M, K] * W[N, K]^T + bias with the chosen epilogue. W is float32 or bf16 (w_bf16), K-major.
+// With ln (GEMV path only; see linear_fuses_layernorm) the rows of X are layer-normalised first.
 cudaError_t launch_linear(cudaStream_t s, const float* x, int ldx, const void* w, int w_bf16,
-                          const float* bias, int M, int N, int K, Epi epi, const EpiArgs& ea);
+                          const float* bias, int M, int N, int K, Epi epi, const EpiArgs& ea,
+                          const LnArgs* ln = nullptr);
+// True when launch_linear can fuse the LayerNorm of its input for this shape.
+bool linear_fuses_layernorm(int M, int N, int K);
 // True when launch_linear(M, N, K) uses the small-M GEMV kernel.
 bool linear_uses_gemv(int M, int N, int K);
 
@@ -68,19 +79,21 @@ cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos
                                 const int* rowmap, const int* next, int* len, int* slot, float* x,
                                 int R, int d);
 
-// LayerNorm over the last dimension with f64 statistics (nn_ops.rs:168-199).
+// LayerNorm over the last dimension with f64 statistics (nn_ops.rs:168-199). Writes y (fp32,
+// optional) and, with planes = 1 (tf32) or 2 (bf16), the split operand planes hi/lo ([rows, d])
+// that the tensor-core GEMM consumes.
 cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const float* gamma,
-                             const float* beta, float* y, int ldy, int rows, int d, float eps);
+                             const float* beta, float* y, int ldy, int rows, int d, float eps,
+                             void* hi = nullptr, void* lo = nullptr, int planes = 0);
 
-// Split-K decode attention over the cache. q: [R, d]; part: [R, heads, splits, head_dim + 2]
-// holding each split's unnormalised output, running max and sum of exponentials.
+// Split-K decode attention over the cache: q [R, d] -> out [R, d]. With splits > 1 each split
+// writes (unnormalised output, max, sum of exponentials) to part [R, heads, splits, head_dim + 2]
+// and the last split of each (row, head) to finish, found through tickets [R * heads] (zero
+// between launches; the kernel re-arms them), merges them in split order.
 cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
                                const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
                                int R, int heads, int head_dim, int slots, float scale, int splits,
-                               int chunk, float* part);
-// Merges the splits: out[i, h*head_dim + e] (out: [R, d]).
-cudaError_t launch_attn_combine(cudaStream_t s, const float* part, int R, int heads, int head_dim,
-                                int splits, float* out);
+                               int chunk, float* part, int* tickets, float* out);
 // Causal prefill attention for `segments` rows; token t of segment j is packed at
 // seg_start[j] + t and sits in cache slot t of row seg_row[j].
 cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,
