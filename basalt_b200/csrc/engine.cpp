@@ -20,6 +20,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -315,6 +316,9 @@ struct Workspace {
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
     int* err = nullptr;                       // tensor-core pipeline error code
     float* tc_part = nullptr;                 // split-K partial products
+    unsigned* bar = nullptr;                  // fused decode step: barrier count, head ticket
+    unsigned long long* best = nullptr;       // fused decode step: per-row packed maximum [8]
+    bst::FusedLayer* fused_layers = nullptr;  // fused decode step: per-layer table [L]
     void *k_cache = nullptr, *v_cache = nullptr;
     size_t kv_layer_elems = 0;
     uint64_t generation = 0;
@@ -364,6 +368,9 @@ class Engine {
     cudaGraphExec_t graph = nullptr;
     std::string graph_key;
     int64_t graph_nodes = 0;
+    int fused_rows = 0, fused_ctas = 0;  // shape the fused decode step was prepared for
+    unsigned fused_bar_base = 0;         // the fused step's barrier count on the device
+    std::vector<bst::FusedLayer> fused_table;
 
     bool profiling = false;
     KernelStats stats[bst::kKernelClassCount];
@@ -469,6 +476,8 @@ class Engine {
     int enqueue_prefill(const StepPlan& p, size_t begin, size_t end);
     int enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens);
     int enqueue_direct(int rows);
+    int prepare_fused(int rows);
+    int enqueue_fused(int rows, int steps, const std::vector<int>& lens, bool history);
     int enqueue_select(Mode mode, int rows, int steps, float temperature, int top_k,
                        bool history);
 };
@@ -716,6 +725,8 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     add(reinterpret_cast<void**>(&ws.step), sizeof(int));
     add(reinterpret_cast<void**>(&ws.done), sizeof(int));
     add(reinterpret_cast<void**>(&ws.err), sizeof(int));
+    add(reinterpret_cast<void**>(&ws.bar), 2 * sizeof(unsigned));
+    add(reinterpret_cast<void**>(&ws.best), 8 * sizeof(unsigned long long));
     {
         // Split planes for the widest tensor-core operand this run can see.
         const int kmax = decoder_family(spec.family) ? std::max(d, F)
@@ -749,6 +760,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
         add(reinterpret_cast<void**>(&ws.part),
             sizeof(float) * static_cast<size_t>(rows) * H * splits * (hd + 2));
         add(reinterpret_cast<void**>(&ws.attn_tickets), sizeof(int) * static_cast<size_t>(rows) * H);
+        add(reinterpret_cast<void**>(&ws.fused_layers), sizeof(bst::FusedLayer) * L);
         ws.kv_layer_elems = static_cast<size_t>(rows) * H * slots * hd;
         const size_t kvb = (kvbf16 ? 2 : 4) * ws.kv_layer_elems * L;
         add(&ws.k_cache, kvb);
@@ -1006,7 +1018,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     const int max_len = std::max(1, ws.slots);
     double sum_len = 0;
     for (int n : lens) sum_len += n;
-    int splits = std::max(1, (296 + R * H - 1) / (R * H));
+    int splits = std::max(1, (592 + R * H - 1) / (R * H));
     int chunk = (max_len + splits - 1) / splits;
     chunk = std::max(32, (chunk + 31) / 32 * 32);
     chunk = std::min(chunk, 1024);
@@ -1101,6 +1113,107 @@ int Engine::enqueue_direct(int rows) {
     return linear(ws.mixed, flat, head_w, head_b, rows, V, flat, Epi::kLogits, lg, "head");
 }
 
+// Whether greedy decode steps of `rows` rows run as one persistent kernel (decode_fused.cu), and
+// the per-layer table it reads. Returns the grid size, or 0 for the kernel-per-operation path.
+// BST_FUSED_DECODE=0 in the environment turns the fused step off.
+int Engine::prepare_fused(int rows) {
+    const char* env = std::getenv("BST_FUSED_DECODE");
+    if (env && std::strcmp(env, "0") == 0) return 0;
+    if (!decoder_family(spec.family) || !bst::fused_decode_supported(rows, d, F, W, hd, wbf16)) {
+        return 0;
+    }
+    if (fused_rows != rows) {
+        fused_ctas = bst::fused_decode_prepare(rows, d, F, V, L, hd, wbf16, kvbf16);
+        fused_rows = rows;
+    }
+    if (fused_ctas <= 0) return 0;
+    const size_t kvb = kvbf16 ? 2 : 4;
+    fused_table.assign(L, bst::FusedLayer{});
+    for (int l = 0; l < L; ++l) {
+        const LayerWeights& lw = layers[l];
+        bst::FusedLayer& f = fused_table[l];
+        f.wqkv = lw.wqkv.w;
+        f.bqkv = lw.bqkv;
+        f.wo = lw.wo.w;
+        f.bo = lw.bo;
+        f.ln1_g = lw.ln1_g;
+        f.ln1_b = lw.ln1_b;
+        f.ln2_g = lw.ln2_g;
+        f.ln2_b = lw.ln2_b;
+        f.w1 = lw.w1.w;
+        f.b1 = lw.b1;
+        f.w2 = lw.w2.w;
+        f.b2 = lw.b2;
+        f.k_cache = static_cast<char*>(ws.k_cache) + l * ws.kv_layer_elems * kvb;
+        f.v_cache = static_cast<char*>(ws.v_cache) + l * ws.kv_layer_elems * kvb;
+    }
+    cudaError_t err = cudaMemcpyAsync(ws.fused_layers, fused_table.data(),
+                                      sizeof(bst::FusedLayer) * L, cudaMemcpyHostToDevice, stream);
+    if (!err) err = cudaMemsetAsync(ws.bar, 0, 2 * sizeof(unsigned), stream);
+    if (!err) err = cudaMemsetAsync(ws.best, 0, 8 * sizeof(unsigned long long), stream);
+    fused_bar_base = 0;
+    if (err) {
+        cuda_fail(err, "preparing the fused decode step");
+        return -1;
+    }
+    return fused_ctas;
+}
+
+int Engine::enqueue_fused(int rows, int steps, const std::vector<int>& lens, bool history) {
+    const double wb = wbf16 ? 2.0 : 4.0, kvb = kvbf16 ? 2.0 : 4.0;
+    bst::FusedStep p;
+    p.R = rows;
+    p.d = d;
+    p.H = H;
+    p.F = F;
+    p.V = V;
+    p.W = W;
+    p.L = L;
+    p.slots = ws.slots;
+    p.steps = steps;
+    p.nchunks = (ws.slots + 31) / 32;
+    p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
+    p.eps = kLayerNormEps;
+    p.len = ws.len;
+    p.next = ws.next;
+    p.tokens = ws.tokens_out;
+    p.window = ws.window;
+    p.step = ws.step;
+    p.done = ws.done;
+    p.rowmap = ws.rowmap_all;
+    p.tok_emb = tok_emb;
+    p.pos_emb = pos_emb;
+    p.lnf_g = lnf_g;
+    p.lnf_b = lnf_b;
+    p.head_w = head_w.w;
+    p.head_b = head_b;
+    p.x = ws.x;
+    p.q = ws.q;
+    p.att = ws.att;
+    p.ffn = ws.ffn;
+    p.logits = ws.logits;
+    p.part = ws.part;
+    p.tickets = ws.attn_tickets;
+    p.bar = ws.bar;
+    p.bar_base = fused_bar_base;
+    p.best = ws.best;
+    p.err = ws.err;
+    p.history = history ? ws.history : nullptr;
+    if (p.nchunks > ws.splits) return fail(BST_PANIC, "decode chunk count exceeds the workspace");
+    // Algorithmic bytes: every weight once, the cache rows attended, activations are negligible.
+    double sum_len = 0;
+    for (int n : lens) sum_len += n;
+    const double params = static_cast<double>(L) * (4.0 * d * d + 2.0 * d * F) + double(V) * d;
+    const double bytes = params * wb + sum_len * 2.0 * d * kvb * L + rows * V * 4.0;
+    const double flops = 2.0 * params * rows + 4.0 * sum_len * d * L;
+    const cudaError_t err = launch(bst::kDecodeStep, bytes, flops, 1, [&] {
+        return bst::launch_decode_fused(stream, p, ws.fused_layers, wbf16, kvbf16, hd, fused_ctas);
+    });
+    if (err) return cuda_fail(err, "fused decode step");
+    fused_bar_base += static_cast<unsigned>(fused_ctas) * bst::fused_decode_barriers(L);
+    return BST_OK;
+}
+
 int Engine::enqueue_select(Mode mode, int rows, int steps, float temperature, int top_k,
                            bool history) {
     cudaError_t err;
@@ -1147,6 +1260,11 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     if (!err) err = cudaMemsetAsync(ws.done, 0, sizeof(int), stream);
     if (!err) err = cudaMemsetAsync(ws.err, 0, sizeof(int), stream);
     if (!err) err = cudaMemsetAsync(ws.len, 0, sizeof(int) * rows, stream);
+    int fused = 0;
+    if (!err && transformer && mode == Mode::kGreedy) {
+        fused = prepare_fused(rows);
+        if (fused < 0) return BST_PANIC;
+    }
     if (!err && mode == Mode::kSample) {
         std::vector<uint64_t> states(rows);
         for (int r = 0; r < rows; ++r) {
@@ -1180,7 +1298,11 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
                 begin = end;
             }
         }
-        if (graphable) {
+        if (fused > 0 && all_decode) {
+            // Small batches: the whole step (selection included) is one persistent kernel.
+            st = enqueue_fused(rows, run_steps, plans[g].decode_len, history);
+            if (st) return st;
+        } else if (graphable) {
             // One CUDA graph per (shape, mode): the step body plus selection reads every
             // step-dependent value (lengths, step counter, RNG state) from device memory.
             char key[160];
@@ -1265,6 +1387,9 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     if (!err) err = cudaStreamSynchronize(stream);
     if (err) return cuda_fail(err, "reading the pipeline status");
     if (pipeline_error) {
+        if (pipeline_error == 11) {
+            return fail(BST_PANIC, "a grid barrier of the fused decode step timed out");
+        }
         return fail(BST_PANIC, "a tensor-core GEMM pipeline wait timed out (stage " +
                                    std::to_string(pipeline_error) + ")");
     }

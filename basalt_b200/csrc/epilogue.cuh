@@ -3,6 +3,7 @@
 
 #include <cuda_bf16.h>
 
+#include "device.cuh"
 #include "kernels.h"
 
 namespace bst {
@@ -62,6 +63,69 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float
         }
     } else if constexpr (E == Epi::kLogits) {
         ea.out[static_cast<size_t>(ea.rowmap[m]) * ea.ldo + n] = v;
+    }
+}
+
+// Block-level LayerNorm of `rows` rows of x into out ([rows][d], shared memory), with the
+// statistics of nn_ops.rs:168-199 (f64 mean and population variance, f32 affine). One row uses
+// every warp of the block; several rows take one warp each.
+__device__ __forceinline__ void layernorm_rows(const float* __restrict__ x, int ldx, int rows, int d,
+                               const LnArgs& ln, float* __restrict__ out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ double red[32];
+    __shared__ double s_stat[2];
+    if (rows == 1) {
+        const int nwarps = static_cast<int>(blockDim.x >> 5);
+        double s = 0.0;
+        for (int k = threadIdx.x; k < d; k += blockDim.x) s = __dadd_rn(s, static_cast<double>(x[k]));
+        s = warp_sum_d(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        if (warp == 0) {
+            const double t = warp_sum_d(lane < nwarps ? red[lane] : 0.0);
+            if (lane == 0) s_stat[0] = __ddiv_rn(t, static_cast<double>(d));
+        }
+        __syncthreads();
+        const double mean = s_stat[0];
+        double v = 0.0;
+        for (int k = threadIdx.x; k < d; k += blockDim.x) {
+            const double delta = __dadd_rn(static_cast<double>(x[k]), -mean);
+            v = __dadd_rn(v, __dmul_rn(delta, delta));
+        }
+        v = warp_sum_d(v);
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            const double t = warp_sum_d(lane < nwarps ? red[lane] : 0.0);
+            if (lane == 0) {
+                const double variance = __ddiv_rn(t, static_cast<double>(d));
+                s_stat[1] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(ln.eps))));
+            }
+        }
+        __syncthreads();
+        const double inverse = s_stat[1];
+        for (int k = threadIdx.x; k < d; k += blockDim.x) {
+            const float nrm = static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(x[k]), -mean), inverse));
+            out[k] = __fadd_rn(__fmul_rn(nrm, ln.gamma[k]), ln.beta[k]);
+        }
+        return;
+    }
+    if (warp >= rows) return;
+    const float* xr = x + static_cast<size_t>(warp) * ldx;
+    float* yr = out + static_cast<size_t>(warp) * d;
+    double s = 0.0;
+    for (int k = lane; k < d; k += 32) s = __dadd_rn(s, static_cast<double>(xr[k]));
+    const double mean = __ddiv_rn(warp_sum_d(s), static_cast<double>(d));
+    double v = 0.0;
+    for (int k = lane; k < d; k += 32) {
+        const double delta = __dadd_rn(static_cast<double>(xr[k]), -mean);
+        v = __dadd_rn(v, __dmul_rn(delta, delta));
+    }
+    const double variance = __ddiv_rn(warp_sum_d(v), static_cast<double>(d));
+    const double inverse = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(ln.eps))));
+    for (int k = lane; k < d; k += 32) {
+        const float nrm = static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(xr[k]), -mean), inverse));
+        yr[k] = __fadd_rn(__fmul_rn(nrm, ln.gamma[k]), ln.beta[k]);
     }
 }
 

@@ -13,6 +13,7 @@
 #include "kernels.h"
 #include "device.cuh"
 #include "epilogue.cuh"
+#include "select.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -27,130 +28,14 @@ const char* kernel_class_name(int cls) {
         "embed",       "layernorm",     "gemv",          "gemm",
         "attn_decode", "attn_combine",  "attn_prefill",  "select_greedy",
         "select_sample", "gather",      "head_last_token", "misc",
-        "split"};
+        "split",       "decode_step"};
     return cls >= 0 && cls < kKernelClassCount ? names[cls] : "unknown";
 }
 
 namespace {
 
-constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMaxChunk = 1024;
 constexpr size_t kSampleSmemLimit = 200 * 1024;
-
-__device__ __forceinline__ float to_f(float v) { return v; }
-__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
-__device__ __forceinline__ float bf16_bits_to_f(uint32_t bits16) {
-    return __uint_as_float(bits16 << 16);
-}
-
-// One 16-byte load of weights/cache, unpacked to floats.
-template <typename T>
-struct Vec16;
-template <>
-struct Vec16<float> {
-    static constexpr int N = 4;
-    __device__ __forceinline__ static void load(const float* p, float* out) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(p));
-        out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
-    }
-};
-template <>
-struct Vec16<__nv_bfloat16> {
-    static constexpr int N = 8;
-    __device__ __forceinline__ static void load(const __nv_bfloat16* p, float* out) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            out[2 * i] = bf16_bits_to_f(w[i] & 0xffffu);
-            out[2 * i + 1] = bf16_bits_to_f(w[i] >> 16);
-        }
-    }
-};
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-    return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
-    return v;
-}
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(kFull, v, o));
-    return v;
-}
-
-// ---------------------------------------------------------------------------------------------
-// GEMV for small M: each output column n is a dot product of W's row n (contiguous, K-major)
-// with up to MT activation rows. KS warps split one column's K range; 8 / KS columns per CTA.
-// Weight rows stream from HBM once with 16-byte coalesced loads; activations hit L1.
-// ---------------------------------------------------------------------------------------------
-// Block-level LayerNorm of `rows` rows of x into out ([rows][d], shared memory), with the
-// statistics of nn_ops.rs:168-199 (f64 mean and population variance, f32 affine). One row uses
-// all eight warps; several rows take one warp each.
-__device__ void layernorm_rows(const float* __restrict__ x, int ldx, int rows, int d,
-                               const LnArgs& ln, float* __restrict__ out) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ double red[8];
-    __shared__ double s_stat[2];
-    if (rows == 1) {
-        double s = 0.0;
-        for (int k = threadIdx.x; k < d; k += blockDim.x) s = __dadd_rn(s, static_cast<double>(x[k]));
-        s = warp_sum_d(s);
-        if (lane == 0) red[warp] = s;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double t = 0.0;
-            for (int w2 = 0; w2 < static_cast<int>(blockDim.x >> 5); ++w2) t = __dadd_rn(t, red[w2]);
-            s_stat[0] = __ddiv_rn(t, static_cast<double>(d));
-        }
-        __syncthreads();
-        const double mean = s_stat[0];
-        double v = 0.0;
-        for (int k = threadIdx.x; k < d; k += blockDim.x) {
-            const double delta = __dadd_rn(static_cast<double>(x[k]), -mean);
-            v = __dadd_rn(v, __dmul_rn(delta, delta));
-        }
-        v = warp_sum_d(v);
-        __syncthreads();
-        if (lane == 0) red[warp] = v;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double t = 0.0;
-            for (int w2 = 0; w2 < static_cast<int>(blockDim.x >> 5); ++w2) t = __dadd_rn(t, red[w2]);
-            const double variance = __ddiv_rn(t, static_cast<double>(d));
-            s_stat[1] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(ln.eps))));
-        }
-        __syncthreads();
-        const double inverse = s_stat[1];
-        for (int k = threadIdx.x; k < d; k += blockDim.x) {
-            const float nrm = static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(x[k]), -mean), inverse));
-            out[k] = __fadd_rn(__fmul_rn(nrm, ln.gamma[k]), ln.beta[k]);
-        }
-        return;
-    }
-    if (warp >= rows) return;
-    const float* xr = x + static_cast<size_t>(warp) * ldx;
-    float* yr = out + static_cast<size_t>(warp) * d;
-    double s = 0.0;
-    for (int k = lane; k < d; k += 32) s = __dadd_rn(s, static_cast<double>(xr[k]));
-    const double mean = __ddiv_rn(warp_sum_d(s), static_cast<double>(d));
-    double v = 0.0;
-    for (int k = lane; k < d; k += 32) {
-        const double delta = __dadd_rn(static_cast<double>(xr[k]), -mean);
-        v = __dadd_rn(v, __dmul_rn(delta, delta));
-    }
-    const double variance = __ddiv_rn(warp_sum_d(v), static_cast<double>(d));
-    const double inverse = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(ln.eps))));
-    for (int k = lane; k < d; k += 32) {
-        const float nrm = static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(xr[k]), -mean), inverse));
-        yr[k] = __fadd_rn(__fmul_rn(nrm, ln.gamma[k]), ln.beta[k]);
-    }
-}
 
 // ---------------------------------------------------------------------------------------------
 // GEMV for small M: each output column n is a dot product of W's row n (contiguous, K-major)
@@ -544,18 +429,30 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __syncthreads();
     const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
     const int sub = lane % LPK, kk = lane / LPK;
-    for (int j0 = warp * KPW; j0 < n; j0 += 4 * KPW) {
-        const int j = j0 + kk;
-        float dot = 0.0f;
-        if (j < n) {
-            float kv[EPV];
-            Vec16<KT>::load(kc + (base + j) * HD + sub * EPV, kv);
+    // Scores: U key groups per round, their 16-byte loads all in flight before any is used.
+    constexpr int U = 4;
+    for (int j0 = warp * KPW; j0 < n; j0 += 4 * KPW * U) {
+        float kv[U][EPV];
 #pragma unroll
-            for (int c = 0; c < EPV; ++c) dot = fmaf(kv[c], qs[sub * EPV + c], dot);
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u * 4 * KPW + kk;
+            if (j < n) {
+                Vec16<KT>::load(kc + (base + j) * HD + sub * EPV, kv[u]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < EPV; ++c) kv[u][c] = 0.0f;
+            }
         }
 #pragma unroll
-        for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(kFull, dot, o);
-        if (sub == 0 && j < n) sc[j] = __fmul_rn(dot, scale);
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u * 4 * KPW + kk;
+            float dot = 0.0f;
+#pragma unroll
+            for (int c = 0; c < EPV; ++c) dot = fmaf(kv[u][c], qs[sub * EPV + c], dot);
+#pragma unroll
+            for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(kFull, dot, o);
+            if (sub == 0 && j < n) sc[j] = __fmul_rn(dot, scale);
+        }
     }
     __syncthreads();
     float mx = -INFINITY;
@@ -575,14 +472,28 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     if (lane == 0) stat[4 + warp] = sum;
     __syncthreads();
     sum = stat[4] + stat[5] + stat[6] + stat[7];
+    // Weighted values: each warp takes every 4th key, UV keys per round with their loads issued
+    // before the multiply-adds.
+    constexpr int UV = 8;
     float o[DPL];
 #pragma unroll
     for (int c = 0; c < DPL; ++c) o[c] = 0.0f;
-    for (int j = warp; j < n; j += 4) {
-        const float p = sc[j];
-        const KT* vr = vc + (base + j) * HD + lane * DPL;
+    for (int j0 = warp; j0 < n; j0 += 4 * UV) {
+        float vv[UV][DPL];
 #pragma unroll
-        for (int c = 0; c < DPL; ++c) o[c] = fmaf(p, to_f(vr[c]), o[c]);
+        for (int u = 0; u < UV; ++u) {
+            const int j = j0 + 4 * u;
+            const KT* vr = vc + (base + min(j, n - 1)) * HD + lane * DPL;
+#pragma unroll
+            for (int c = 0; c < DPL; ++c) vv[u][c] = to_f(vr[c]);
+        }
+#pragma unroll
+        for (int u = 0; u < UV; ++u) {
+            const int j = j0 + 4 * u;
+            const float p = j < n ? sc[j] : 0.0f;
+#pragma unroll
+            for (int c = 0; c < DPL; ++c) o[c] = fmaf(p, vv[u][c], o[c]);
+        }
     }
 #pragma unroll
     for (int c = 0; c < DPL; ++c) red[warp * HD + lane * DPL + c] = o[c];
@@ -716,37 +627,6 @@ __global__ __launch_bounds__(128) void k_attn_prefill(
 // ---------------------------------------------------------------------------------------------
 // Token selection and step bookkeeping.
 // ---------------------------------------------------------------------------------------------
-// Writes the chosen token, shifts the row's window (TextEngine.push, TextEngine.java:387-390) and
-// advances the step counter once the last row of the step is done.
-__device__ void finish_row(int r, int token, int g, int rows, int W, int steps, int* step,
-                           int* done, int* tokens, int* next, int* window) {
-    int* win = window + static_cast<size_t>(r) * W;
-    constexpr int kPerThread = 8;
-    int carry[kPerThread];
-#pragma unroll
-    for (int c = 0; c < kPerThread; ++c) {
-        const int t = threadIdx.x + c * blockDim.x;
-        carry[c] = t + 1 < W ? win[t + 1] : token;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < kPerThread; ++c) {
-        const int t = threadIdx.x + c * blockDim.x;
-        if (t < W) win[t] = carry[c];
-    }
-    if (threadIdx.x == 0) {
-        tokens[static_cast<size_t>(r) * steps + g] = token;
-        next[r] = token;
-        __threadfence();
-        const int prev = atomicAdd(done, 1);
-        if (prev == rows - 1) {
-            *done = 0;
-            *step = g + 1;
-            __threadfence();
-        }
-    }
-}
-
 // TextEngine.argmax (TextEngine.java:392-400): strict '>' so the first maximum wins.
 __global__ __launch_bounds__(256) void k_select_greedy(const float* __restrict__ logits, int V,
                                                        int W, int steps, int rows, int* step,
@@ -755,49 +635,10 @@ __global__ __launch_bounds__(256) void k_select_greedy(const float* __restrict__
     pdl_trigger();
     pdl_wait();
     const int r = blockIdx.x;
-    const float* lr = logits + static_cast<size_t>(r) * V;
     __shared__ int s_step;
-    __shared__ float s_val[8];
-    __shared__ int s_idx[8];
     if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile int*>(step);
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float x = lr[v];
-        if (isnan(x)) continue;
-        if (x > best || (x == best && v < bi)) {
-            best = x;
-            bi = v;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(kFull, best, o);
-        const int oi = __shfl_xor_sync(kFull, bi, o);
-        if (ov > best || (ov == best && oi < bi)) {
-            best = ov;
-            bi = oi;
-        }
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        s_val[warp] = best;
-        s_idx[warp] = bi;
-    }
-    __syncthreads();
-    __shared__ int s_token;
-    if (threadIdx.x == 0) {
-        for (int w2 = 1; w2 < static_cast<int>(blockDim.x >> 5); ++w2) {
-            if (s_val[w2] > best || (s_val[w2] == best && s_idx[w2] < bi)) {
-                best = s_val[w2];
-                bi = s_idx[w2];
-            }
-        }
-        // A NaN first score is never replaced (no value compares greater than it).
-        s_token = (isnan(lr[0]) || bi == 0x7fffffff) ? 0 : bi;
-    }
-    __syncthreads();
-    finish_row(r, s_token, s_step, rows, W, steps, step, done, tokens, next, window);
+    const int token = block_argmax(logits + static_cast<size_t>(r) * V, V);
+    finish_row(r, token, s_step, rows, W, steps, step, done, tokens, next, window);
 }
 
 // java.util.Random step and nextDouble (JDK specification).

@@ -24,7 +24,8 @@ enum KernelClass : int {
     kHeadLastToken = 10,
     kMisc = 11,
     kSplit = 12,
-    kKernelClassCount = 13,
+    kDecodeStep = 13,
+    kKernelClassCount = 14,
 };
 
 const char* kernel_class_name(int cls);
@@ -165,6 +166,57 @@ size_t tc_part_bytes(int M, int N, int K, int w_bf16);
 // Copies this step's logits [rows, V] to history[r][*step][v] (history: [rows, steps, V]).
 cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,
                                 const int* step, float* history);
+
+// ---- whole decode step in one persistent kernel (decode_fused.cu) ----
+// One layer's weights and cache for the fused step; an array of these lives in device memory.
+struct FusedLayer {
+    const void* wqkv = nullptr;  // [3d, d]
+    const float* bqkv = nullptr;
+    const void* wo = nullptr;    // [d, d]
+    const float* bo = nullptr;
+    const float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+    const void* w1 = nullptr;    // [F, d]
+    const float* b1 = nullptr;
+    const void* w2 = nullptr;    // [d, F]
+    const float* b2 = nullptr;
+    void *k_cache = nullptr, *v_cache = nullptr;  // [R][H][slots][hd]
+};
+
+// Everything one greedy decode step of R rows reads and writes. Rows are cache rows 0..R-1;
+// len[i] is row i's cache length before the step (the new key goes to slot len[i], and the
+// select phase adds one).
+struct FusedStep {
+    int R = 0, d = 0, H = 0, F = 0, V = 0, W = 0, L = 0, slots = 0, steps = 0, nchunks = 0;
+    float scale = 0.0f, eps = 0.0f;
+    int *len = nullptr, *next = nullptr, *tokens = nullptr, *window = nullptr;
+    int *step = nullptr, *done = nullptr;
+    const int* rowmap = nullptr;  // identity [R]
+    const void *tok_emb = nullptr, *pos_emb = nullptr;
+    const float *lnf_g = nullptr, *lnf_b = nullptr;
+    const void* head_w = nullptr;  // [V, d]
+    const float* head_b = nullptr;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *ffn = nullptr, *logits = nullptr;
+    float* part = nullptr;         // [R, H, nchunks, hd + 2]
+    int* tickets = nullptr;        // [R * H], zero between launches
+    unsigned* bar = nullptr;       // [0] grid barrier arrivals (only grows), [1] head ticket
+    unsigned bar_base = 0;         // bar[0] when this launch starts
+    unsigned long long* best = nullptr;  // [R] packed per-row maximum, zero between launches
+    int* err = nullptr;            // non-zero when a grid barrier timed out
+    float* history = nullptr;      // optional [R, steps, V] logits
+    unsigned table_offset = 0;                     // layer table in shared memory (set by launch)
+    unsigned wstage_offset = 0, wstage_bytes = 0;  // weight stage in shared memory (set by launch)
+};
+
+// True when the fused step handles this shape (R <= 8, head_dim 32/64/128, window <= 4096).
+bool fused_decode_supported(int R, int d, int F, int W, int head_dim, int w_bf16);
+// Prepares the kernel for this shape on the current device and returns the grid size (one CTA per
+// SM), or 0 when its shared memory does not fit or the device cannot co-schedule it. Call outside
+// stream capture.
+int fused_decode_prepare(int R, int d, int F, int V, int L, int head_dim, int w_bf16, int kv_bf16);
+// Grid barriers one launch passes (bar[0] grows by this times the grid size).
+int fused_decode_barriers(int layers);
+cudaError_t launch_decode_fused(cudaStream_t s, const FusedStep& p, const FusedLayer* layers,
+                                int w_bf16, int kv_bf16, int head_dim, int ctas);
 
 cudaError_t launch_fill_int(cudaStream_t s, int* p, int value, int count);
 cudaError_t launch_iota(cudaStream_t s, int* p, int count);

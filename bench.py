@@ -210,12 +210,16 @@ def batch1(local, steps, warmup):
     gemv_gbs = gemv["bytes"] / (gemv["ms"] / 1000.0) / 1e9 if gemv and gemv["ms"] else None
     attn = prof.get("attn_decode")
     attn_gbs = attn["bytes"] / (attn["ms"] / 1000.0) / 1e9 if attn and attn["ms"] else None
+    step = prof.get("decode_step")
+    step_gbs = step["bytes"] / (step["ms"] / 1000.0) / 1e9 if step and step["ms"] else None
     engine.close()
     return {"workload": w.name, "tokens_per_s": w.steps / (full_ms / 1000.0),
             "ms_per_call": full_ms, "prefill_ms": prefill_ms,
             "decode_ms_per_token": per_token_ms,
             "gemv_GBps": gemv_gbs, "gemv_frac": gemv_gbs / hbm if gemv_gbs else None,
-            "attn_decode_GBps": attn_gbs, "peak_source": src, "kernels": kernels}
+            "attn_decode_GBps": attn_gbs,
+            "decode_step_GBps": step_gbs, "decode_step_frac": step_gbs / hbm if step_gbs else None,
+            "peak_source": src, "kernels": kernels}
 
 
 def run_reference(args, rank, world):
