@@ -183,17 +183,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* smem_dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
@@ -231,12 +220,14 @@ struct WStage {
     uint64_t* bar;          // mbarrier (shared), one phase per issued copy
     unsigned char* buf;     // weight rows (shared)
     unsigned cap;           // bytes
-    float* bias;            // [columns] (shared)
+    float* bias;            // [columns + 4] (shared), column c0 + j at bias[j + bias_off]
     float* lnp;             // gamma [K], beta [K] (shared)
     int* abort_flag;        // shared
     int* err;
     unsigned parity;        // phase the next wait expects
     int cols;               // weight rows of the current projection held in buf
+    int bias_off;           // bias block starts bias_off floats before column c0
+    bool pending;           // a copy was issued and not yet waited for
 };
 
 // Issues the stage of the projection Y[R, N] = X W^T (W [N, K] of WT) for this CTA.
@@ -247,32 +238,34 @@ __device__ __forceinline__ void stage_issue(const void* w, const float* bias, in
     column_block(N, &c0, &c1);
     const size_t row_bytes = static_cast<size_t>(K) * sizeof(WT);
     st.cols = c1 > c0 ? min(c1 - c0, static_cast<int>(st.cap / row_bytes)) : 0;
+    st.bias_off = c0 & 3;
+    st.pending = c1 > c0;
     if (c1 <= c0) return;  // uniform over the CTA
-    // Every thread is done with the previous projection's stage: hand the buffer to the TMA unit.
+    // Every thread is done with the previous projection's stage: hand it to the TMA unit. All of
+    // it arrives by bulk copies on one mbarrier: the weight rows, the LayerNorm parameters and the
+    // bias block (its start rounded down, its end up, to 16 bytes).
     __syncthreads();
-    if (threadIdx.x == 0 && st.cols > 0) {
+    if (threadIdx.x == 0) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const uint32_t bytes = static_cast<uint32_t>(st.cols * row_bytes);
-        mbar_expect_tx(st.bar, bytes);
-        bulk_load(st.buf, static_cast<const WT*>(w) + static_cast<size_t>(c0) * K, bytes, st.bar);
-    }
-    if (ln_gamma) {
-        const int q = K / 4;
-        for (int c = threadIdx.x; c < 2 * q; c += kThreads) {
-            cp_async16(st.lnp + 4 * c, c < q ? ln_gamma + 4 * c : ln_beta + 4 * (c - q));
+        const uint32_t wbytes = static_cast<uint32_t>(st.cols * row_bytes);
+        const uint32_t lbytes = ln_gamma ? static_cast<uint32_t>(K) * 4u : 0u;
+        const uint32_t bbytes = bias ? static_cast<uint32_t>((c1 - c0 + st.bias_off + 3) / 4 * 16) : 0u;
+        mbar_expect_tx(st.bar, wbytes + 2 * lbytes + bbytes);
+        if (wbytes) {
+            bulk_load(st.buf, static_cast<const WT*>(w) + static_cast<size_t>(c0) * K, wbytes, st.bar);
         }
+        if (lbytes) {
+            bulk_load(st.lnp, ln_gamma, lbytes, st.bar);
+            bulk_load(st.lnp + K, ln_beta, lbytes, st.bar);
+        }
+        if (bbytes) bulk_load(st.bias, bias + (c0 - st.bias_off), bbytes, st.bar);
     }
-    if (bias) {
-        for (int c = threadIdx.x; c < c1 - c0; c += kThreads) cp_async4(st.bias + c, bias + c0 + c);
-    }
-    cp_async_commit();
 }
 
 // Waits for the stage issued by stage_issue (bounded; on expiry records code 12, waits once more
 // for the copy to land and lets the next grid barrier end the kernel).
 __device__ __forceinline__ void stage_wait(WStage& st) {
-    cp_async_wait_all();
-    if (st.cols > 0) {
+    if (st.pending) {
         if (!mbar_try_wait(st.bar, st.parity)) {
             uint64_t start = global_ns();
             bool late = false;
@@ -287,6 +280,7 @@ __device__ __forceinline__ void stage_wait(WStage& st) {
             }
         }
         st.parity ^= 1u;
+        st.pending = false;
     }
 }
 
@@ -374,7 +368,7 @@ __device__ __forceinline__ void gemv(const float* x, int ldx, bool staged, bool 
         stage_wait(st);
         __syncthreads();
         const LnArgs lns{st.lnp, st.lnp + K, cx.eps};
-        layernorm_rows(cx.xraw, K, RT == 1 ? 1 : R, K, lns, xs);
+        layernorm_rows(cx.xraw, K, RT == 1 ? 1 : R, K, lns, xs, true);
     } else {
         stage_rows(x, ldx, R, K, xs);
         stage_wait(st);
@@ -436,7 +430,7 @@ __device__ __forceinline__ void gemv(const float* x, int ldx, bool staged, bool 
             storer = act && threadIdx.x % pl.gs == 0;
         }
         if (storer) {
-            const float b = has_bias ? st.bias[col - pl.c0] : 0.0f;
+            const float b = has_bias ? st.bias[col - pl.c0 + st.bias_off] : 0.0f;
 #pragma unroll
             for (int i = 0; i < RT; ++i) {
                 if (i < R) store_out(epi, ea, sk, pl.c0, i, col, has_bias ? __fadd_rn(acc[i], b) : acc[i]);
@@ -467,7 +461,7 @@ __device__ __forceinline__ void attention_phase(const float* q, const KT* kc, co
     constexpr int LB = DV < 64 / VE ? DV : 64 / VE;    // loads in flight per lane: 64 floats
     constexpr int PB = KPL < 64 / VE ? KPL : 64 / VE;
     constexpr int DPL = HD / 32;
-    constexpr int MB = 8;  // chunks per batch of merge loads
+    constexpr int MB = 32 / DPL;  // merge loads in flight per lane: 32 floats
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = heads * HD;
     float* qw = qslot + warp * HD;
@@ -483,11 +477,19 @@ __device__ __forceinline__ void attention_phase(const float* q, const KT* kc, co
         const int start = c * kChunk;
         const int n = min(kChunk, T - start);
         const size_t base = (static_cast<size_t>(i) * heads + h) * slots + start;
-        // This lane's key (the last key again for lanes past the chunk) and the query, together.
+        // This lane's key (the last key again for lanes past the chunk) and the query, together;
+        // the chunk's values are asked into L2 at the same time.
         const KT* kr = kc + (base + min(lane, n - 1)) * HD;
         float kv[LB][VE];
 #pragma unroll
         for (int e = 0; e < LB; ++e) load_cg16(kr + e * VE, kv[e]);
+        {
+            const char* vbase = reinterpret_cast<const char*>(vc + base * HD);
+            const int vlines = (n * HD * static_cast<int>(sizeof(KT)) + 127) / 128;
+            for (int ln = lane; ln < vlines; ln += 32) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(vbase + ln * 128));
+            }
+        }
         for (int e = lane; e < HD; e += 32) qw[e] = __ldcg(q + static_cast<size_t>(i) * d + h * HD + e);
         __syncwarp();
         float dot = 0.0f;
@@ -543,52 +545,61 @@ __device__ __forceinline__ void attention_phase(const float* q, const KT* kc, co
             mine[HD] = m;
             mine[HD + 1] = l;
         }
-        __threadfence();
+        // Publish the partial: the ticket is a release (it orders the warp's stores above, which
+        // __syncwarp orders before it) and an acquire for the warp that merges.
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(&tickets[i * heads + h], 1) == nck - 1;
+        if (lane == 0) {
+            last = atom_add_acq_rel(reinterpret_cast<unsigned*>(&tickets[i * heads + h]), 1) ==
+                   static_cast<unsigned>(nck - 1);
+        }
         last = __shfl_sync(kFull, last, 0);
         if (last) {
-            __threadfence();
+            __syncwarp();  // orders every lane's loads below after lane 0's acquire
             const float* all = part + static_cast<size_t>(i * heads + h) * nchunks * (HD + 2);
-            // Chunk statistics, lanes over chunks: the common case (up to 32 chunks) keeps each
-            // lane's chunk max in a register; beyond that the groups of 32 are re-read from L2.
-            const float m0 = lane < nck ? __ldcg(all + lane * (HD + 2) + HD) : -INFINITY;
-            const float l0 = lane < nck ? __ldcg(all + lane * (HD + 2) + HD + 1) : 0.0f;
-            float M = m0;
-            for (int z = 32 + lane; z < nck; z += 32) M = fmaxf(M, __ldcg(all + z * (HD + 2) + HD));
-            M = warp_max(M);
-            float Lp = lane < nck ? l0 * expf(m0 - M) : 0.0f;
-            for (int z = 32 + lane; z < nck; z += 32) {
-                Lp = fmaf(__ldcg(all + z * (HD + 2) + HD + 1), expf(__ldcg(all + z * (HD + 2) + HD) - M), Lp);
-            }
-            const float L = warp_sum(Lp);
+            // Every load of the merge in one round for up to 32 chunks: lane z reads chunk z's
+            // (max, sum), and each lane its DPL dimensions of every chunk; more chunks take further
+            // rounds of 32.
+            float M = -INFINITY, L = 0.0f;
             float O[DPL];
 #pragma unroll
             for (int cc = 0; cc < DPL; ++cc) O[cc] = 0.0f;
             for (int zb = 0; zb < nck; zb += 32) {
-                const int zl = zb + lane;
-                const float wz = zl >= nck ? 0.0f
-                                 : zb == 0 ? expf(m0 - M) : expf(__ldcg(all + zl * (HD + 2) + HD) - M);
                 const int zn = min(32, nck - zb);
-#pragma unroll 1
-                for (int z0 = 0; z0 < zn; z0 += MB) {
-                    float ov[MB][DPL];
+                const float mz = lane < zn ? __ldcg(all + (zb + lane) * (HD + 2) + HD) : -INFINITY;
+                const float lz = lane < zn ? __ldcg(all + (zb + lane) * (HD + 2) + HD + 1) : 0.0f;
+                float ov[MB][DPL];
 #pragma unroll
-                    for (int t = 0; t < MB; ++t) {
-                        const int z = zb + min(z0 + t, zn - 1);
+                for (int t = 0; t < MB; ++t) {
+                    const int z = zb + min(t, zn - 1);
 #pragma unroll
-                        for (int cc = 0; cc < DPL; ++cc) ov[t][cc] = __ldcg(all + z * (HD + 2) + lane * DPL + cc);
-                    }
+                    for (int cc = 0; cc < DPL; ++cc) ov[t][cc] = __ldcg(all + z * (HD + 2) + lane * DPL + cc);
+                }
+                // rescale what earlier rounds accumulated to the new running maximum
+                const float Mn = fmaxf(M, warp_max(mz));
+                const float carry = M == -INFINITY ? 0.0f : expf(M - Mn);
+                const float wz = lane < zn ? expf(mz - Mn) : 0.0f;
+                L = fmaf(L, carry, warp_sum(lz * wz));
 #pragma unroll
-                    for (int t = 0; t < MB; ++t) {
-                        const float wt = __shfl_sync(kFull, wz, (z0 + t) & 31);
-                        if (z0 + t < zn) {
+                for (int cc = 0; cc < DPL; ++cc) O[cc] *= carry;
 #pragma unroll
-                            for (int cc = 0; cc < DPL; ++cc) O[cc] = fmaf(ov[t][cc], wt, O[cc]);
+                for (int t0 = 0; t0 < 32; t0 += MB) {
+                    if (t0 > 0) {
+#pragma unroll
+                        for (int t = 0; t < MB; ++t) {
+                            const int z = zb + min(t0 + t, zn - 1);
+#pragma unroll
+                            for (int cc = 0; cc < DPL; ++cc) ov[t][cc] = __ldcg(all + z * (HD + 2) + lane * DPL + cc);
                         }
                     }
+#pragma unroll
+                    for (int t = 0; t < MB; ++t) {
+                        const float wt = __shfl_sync(kFull, wz, t0 + t);
+#pragma unroll
+                        for (int cc = 0; cc < DPL; ++cc) O[cc] = fmaf(ov[t][cc], wt, O[cc]);
+                    }
                 }
+                M = Mn;
             }
 #pragma unroll
             for (int cc = 0; cc < DPL; ++cc) {
@@ -662,7 +673,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
     float* xraw = xs + static_cast<size_t>(R) * max(d, F);   // [R][d]
     float* lnp = xraw + static_cast<size_t>(R) * d;          // LayerNorm gamma, beta [2][d]
     float* xown = lnp + 2 * static_cast<size_t>(d);          // [R][own_ld]
-    float* bsm = xown + static_cast<size_t>(R) * own_ld;     // [bias_cap]
+    float* bsm = xown + ((R * own_ld + 3) & ~3);             // [bias_cap], 16-byte aligned
     FusedLayer* lt = reinterpret_cast<FusedLayer*>(reinterpret_cast<unsigned char*>(smem) + p.table_offset);
     unsigned char* wbuf = reinterpret_cast<unsigned char*>(smem) + p.wstage_offset;
     if (threadIdx.x == 0) {
@@ -685,7 +696,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
         for (int i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
     }
     GridSync gsync{p.bar, p.bar_base, p.err, &abort_flag};
-    WStage st{&s_wbar, wbuf, p.wstage_bytes, bsm, lnp, &abort_flag, p.err, 0u, 0};
+    WStage st{&s_wbar, wbuf, p.wstage_bytes, bsm, lnp, &abort_flag, p.err, 0u, 0, 0, false};
     const Ctx cx{xs, xraw, R, p.eps};
     __syncthreads();
     {
@@ -810,8 +821,9 @@ Layout fused_layout(int R, int d, int F, int V, int L, int ctas) {
     const size_t own_ld = (d + ctas - 1) / ctas;
     const size_t widest = std::max({static_cast<size_t>(3) * d, static_cast<size_t>(F),
                                     static_cast<size_t>(V)});
-    const size_t bias_cap = ((widest + ctas - 1) / ctas + 3) / 4 * 4;
-    const size_t floats = static_cast<size_t>(R) * (std::max(d, F) + d + own_ld) + 2 * d + bias_cap;
+    const size_t bias_cap = ((widest + ctas - 1) / ctas + 3) / 4 * 4 + 4;
+    const size_t floats = static_cast<size_t>(R) * (std::max(d, F) + d) + 2 * d +
+                          (R * own_ld + 3) / 4 * 4 + bias_cap;
     lay.table_offset = (floats * sizeof(float) + 15) / 16 * 16;
     lay.stage_offset = (lay.table_offset + sizeof(FusedLayer) * L + 127) / 128 * 128;
     if (lay.stage_offset > kSmemLimit) return lay;

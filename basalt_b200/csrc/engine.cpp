@@ -314,6 +314,7 @@ struct Workspace {
     float* history = nullptr;                 // per-step logits, when requested
     bool has_history = false;
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
+    void *ys_hi = nullptr, *ys_lo = nullptr;  // planes a producer writes for the next projection
     int* err = nullptr;                       // tensor-core pipeline error code
     float* tc_part = nullptr;                 // split-K partial products
     unsigned* bar = nullptr;                  // fused decode step: barrier count, head ticket
@@ -472,7 +473,12 @@ class Engine {
     void plan(const std::vector<int32_t>& windows, int rows, int steps,
               std::vector<StepPlan>* plans, int* max_slots, int* max_tokens) const;
     int linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N, int K,
-               Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln = nullptr);
+               Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln = nullptr,
+               bool presplit = false);
+    // Whether linear() takes the tensor-core path for this shape, and the operand planes a
+    // producer should write for it (into ws.ys_*; none when the GEMV path consumes fp32).
+    bool linear_on_tc(const Matrix& m, int M, int N, int K) const;
+    bst::PlaneOut planes_for(const Matrix& m, int M, int N, int K) const;
     int enqueue_prefill(const StepPlan& p, size_t begin, size_t end);
     int enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens);
     int enqueue_direct(int rows);
@@ -630,6 +636,9 @@ int Engine::upload_weights() {
 
     cudaError_t err = cudaSetDevice(device);
     if (err != cudaSuccess) return cuda_fail(err, "cudaSetDevice");
+    // Slack after the last tensor: the fused decode step copies bias blocks with their ends
+    // rounded up to 16 bytes.
+    total += 256;
     if (weights.ptr && weights.bytes < total) {
         cudaFree(weights.ptr);
         weights = Buffer{};
@@ -734,6 +743,8 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
         const size_t plane = bst::tc_split_bytes(act_rows, kmax, wbf16);
         add(&ws.xs_hi, plane);
         add(&ws.xs_lo, plane);
+        add(&ws.ys_hi, plane);
+        add(&ws.ys_lo, plane);
         add(reinterpret_cast<void**>(&ws.tc_part), bst::tc_part_bytes_max());
     }
     add(reinterpret_cast<void**>(&ws.rng), sizeof(uint64_t) * rows);
@@ -855,16 +866,37 @@ void Engine::plan(const std::vector<int32_t>& windows, int rows, int steps,
 
 // One projection: GEMV (M <= 8) or tiled FFMA for odd shapes, otherwise split the operand and
 // run the tcgen05 GEMM.
+bool Engine::linear_on_tc(const Matrix& m, int M, int N, int K) const {
+    return bst::tc_usable(M, N, K, wbf16) && (wbf16 || m.hi);
+}
+
+bst::PlaneOut Engine::planes_for(const Matrix& m, int M, int N, int K) const {
+    bst::PlaneOut po;
+    if (linear_on_tc(m, M, N, K)) {
+        po.hi = ws.ys_hi;
+        po.lo = ws.ys_lo;
+        po.planes = wbf16 ? 2 : 1;
+        po.ld = K;
+    }
+    return po;
+}
+
 int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N,
-                   int K, Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln) {
+                   int K, Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln,
+                   bool presplit) {
     const double wb = wbf16 ? 2.0 : 4.0;
     cudaError_t err;
-    if (bst::tc_usable(M, N, K, wbf16) && (wbf16 || m.hi)) {
-        // Tensor-core path: the operand is split into hi/lo planes, by the LayerNorm when one
-        // precedes the projection, otherwise by a split pass.
+    if (linear_on_tc(m, M, N, K)) {
+        // Tensor-core path: the operand is split into hi/lo planes, by its producer (presplit:
+        // already in ws.ys_*), by the LayerNorm when one precedes the projection, or by a split
+        // pass.
         const double plane = static_cast<double>(bst::tc_split_bytes(M, K, wbf16));
         const int planes = wbf16 ? 2 : 1;
-        if (ln) {
+        const void* a_hi = presplit ? ws.ys_hi : ws.xs_hi;
+        const void* a_lo = presplit ? ws.ys_lo : ws.xs_lo;
+        if (presplit) {
+            err = cudaSuccess;
+        } else if (ln) {
             err = launch(bst::kLayerNorm, M * K * 4.0 + 2 * plane, 0, 1, [&] {
                 return bst::launch_layernorm(stream, x, ldx, ln->gamma, ln->beta, nullptr, 0, M,
                                              K, ln->eps, ws.xs_hi, ws.xs_lo, planes);
@@ -881,7 +913,7 @@ int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, 
             bst::tc_plan(M, N, K, wbf16, bst::tc_part_bytes_max(), nullptr) > 1 ? 2 : 1;
         err = launch(bst::kGemm, wbytes + 2 * plane + static_cast<double>(M) * N * 4.0,
                      2.0 * M * N * K, kernels, [&] {
-                         return bst::launch_gemm_tc(stream, ws.xs_hi, ws.xs_lo,
+                         return bst::launch_gemm_tc(stream, a_hi, a_lo,
                                                     wbf16 ? m.w : m.hi, m.lo, wbf16, bias, M, N,
                                                     K, epi, ea, ws.err, ws.tc_part,
                                                     bst::tc_part_bytes_max());
@@ -974,25 +1006,29 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         qkv.kv_bf16 = kvbf16;
         st = linear(ws.x, d, lw.wqkv, lw.bqkv, T, 3 * d, d, Epi::kQkv, qkv, "qkv projection", &ln1);
         if (st) return st;
+        const bst::PlaneOut att_planes = planes_for(lw.wo, T, d, d);
         st = check(launch(bst::kAttnPrefill, attn_bytes, attn_flops, 1, [&] {
                        return bst::launch_attn_prefill(stream, ws.q, qkv.k_cache, qkv.v_cache,
                                                        kvbf16, ws.seg_row, ws.seg_start,
                                                        ws.seg_len, segs, max_len, H, hd, slots,
-                                                       scale, ws.att);
+                                                       scale, ws.att, att_planes);
                    }), "prefill attention");
         if (st) return st;
         EpiArgs res;
         res.out = ws.x;
         res.ldo = d;
-        st = linear(ws.att, d, lw.wo, lw.bo, T, d, d, Epi::kResidual, res, "output projection");
+        st = linear(ws.att, d, lw.wo, lw.bo, T, d, d, Epi::kResidual, res, "output projection",
+                    nullptr, att_planes.planes != 0);
         if (st) return st;
         const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
+        act.split = planes_for(lw.w2, T, d, F);
         st = linear(ws.x, d, lw.w1, lw.b1, T, F, d, Epi::kGelu, act, "ffn1", &ln2);
         if (st) return st;
-        st = linear(ws.ffn, F, lw.w2, lw.b2, T, d, F, Epi::kResidual, res, "ffn2");
+        st = linear(ws.ffn, F, lw.w2, lw.b2, T, d, F, Epi::kResidual, res, "ffn2", nullptr,
+                    act.split.planes != 0);
         if (st) return st;
     }
     st = check(launch(bst::kGather, segs * d * 8.0, 0, 1, [&] {
@@ -1048,25 +1084,29 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         st = linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv, "qkv projection", &ln1);
         if (st) return st;
         const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0;
+        const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
         st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * sum_len * d, 1, [&] {
                        return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
                                                       kvbf16, rowmap, ws.len, R, H, hd, slots,
                                                       scale, splits, chunk, ws.part,
-                                                      ws.attn_tickets, ws.att);
+                                                      ws.attn_tickets, ws.att, att_planes);
                    }), "decode attention");
         if (st) return st;
         EpiArgs res;
         res.out = ws.x;
         res.ldo = d;
-        st = linear(ws.att, d, lw.wo, lw.bo, R, d, d, Epi::kResidual, res, "output projection");
+        st = linear(ws.att, d, lw.wo, lw.bo, R, d, d, Epi::kResidual, res, "output projection",
+                    nullptr, att_planes.planes != 0);
         if (st) return st;
         const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
+        act.split = planes_for(lw.w2, R, d, F);
         st = linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1", &ln2);
         if (st) return st;
-        st = linear(ws.ffn, F, lw.w2, lw.b2, R, d, F, Epi::kResidual, res, "ffn2");
+        st = linear(ws.ffn, F, lw.w2, lw.b2, R, d, F, Epi::kResidual, res, "ffn2", nullptr,
+                    act.split.planes != 0);
         if (st) return st;
     }
     const bst::LnArgs lnf{lnf_g, lnf_b, kLayerNormEps};

@@ -35,8 +35,15 @@ template <Epi E>
 __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float v) {
     if constexpr (E == Epi::kStore) {
         ea.out[static_cast<size_t>(m) * ea.ldo + n] = v;
+        if (ea.split.planes) {
+            store_split(v, ea.split.planes, ea.split.hi, ea.split.lo, static_cast<size_t>(m) * ea.split.ld + n);
+        }
     } else if constexpr (E == Epi::kGelu) {
-        ea.out[static_cast<size_t>(m) * ea.ldo + n] = gelu_ref(v);
+        const float g = gelu_ref(v);
+        ea.out[static_cast<size_t>(m) * ea.ldo + n] = g;
+        if (ea.split.planes) {
+            store_split(g, ea.split.planes, ea.split.hi, ea.split.lo, static_cast<size_t>(m) * ea.split.ld + n);
+        }
     } else if constexpr (E == Epi::kResidual) {
         float* p = ea.out + static_cast<size_t>(m) * ea.ldo + n;
         *p = __fadd_rn(*p, v);
@@ -68,13 +75,13 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float
 
 // Block-level LayerNorm of `rows` rows of x into out ([rows][d], shared memory), with the
 // statistics of nn_ops.rs:168-199 (f64 mean and population variance, f32 affine). One row uses
-// every warp of the block; several rows take one warp each.
+// every warp of the block unless `warp_rows` is set; several rows take one warp each.
 __device__ __forceinline__ void layernorm_rows(const float* __restrict__ x, int ldx, int rows, int d,
-                               const LnArgs& ln, float* __restrict__ out) {
+                               const LnArgs& ln, float* __restrict__ out, bool warp_rows = false) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ double red[32];
     __shared__ double s_stat[2];
-    if (rows == 1) {
+    if (rows == 1 && !warp_rows) {
         const int nwarps = static_cast<int>(blockDim.x >> 5);
         double s = 0.0;
         for (int k = threadIdx.x; k < d; k += blockDim.x) s = __dadd_rn(s, static_cast<double>(x[k]));

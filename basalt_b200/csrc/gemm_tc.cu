@@ -313,13 +313,16 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int 
                                 const float* __restrict__ bias, EpiArgs ea) {
     pdl_trigger();
     pdl_wait();
+    // Grid: x over column blocks of 256, y over rows (strided).
     const size_t total = static_cast<size_t>(M) * N;
-    for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
-         e += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const float b = bias ? bias[n] : 0.0f;
+    for (int m = blockIdx.y; m < M; m += gridDim.y) {
+        const size_t e = static_cast<size_t>(m) * N + n;
         float v = 0.0f;
         for (int z = 0; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
-        const int m = static_cast<int>(e / N), n = static_cast<int>(e % N);
-        epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, bias[n]) : v);
+        epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, b) : v);
     }
 }
 
@@ -328,12 +331,13 @@ __global__ void k_split_tf32(const float* __restrict__ x, int ldx, int M, int K,
                              float* __restrict__ hi, float* __restrict__ lo) {
     pdl_trigger();
     pdl_wait();
-    const size_t total = static_cast<size_t>(M) * K;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int m = static_cast<int>(i / K), k = static_cast<int>(i % K);
+    // Grid: x over column blocks of 256, y over rows (strided).
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= K) return;
+    for (int m = blockIdx.y; m < M; m += gridDim.y) {
         const float v = x[static_cast<size_t>(m) * ldx + k];
         const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        const size_t i = static_cast<size_t>(m) * K + k;
         hi[i] = h;
         lo[i] = __fsub_rn(v, h);
     }
@@ -343,12 +347,12 @@ __global__ void k_split_bf16(const float* __restrict__ x, int ldx, int M, int K,
                              __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
     pdl_trigger();
     pdl_wait();
-    const size_t total = static_cast<size_t>(M) * K;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int m = static_cast<int>(i / K), k = static_cast<int>(i % K);
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= K) return;
+    for (int m = blockIdx.y; m < M; m += gridDim.y) {
         const float v = x[static_cast<size_t>(m) * ldx + k];
         const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        const size_t i = static_cast<size_t>(m) * K + k;
         hi[i] = h;
         lo[i] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
     }
@@ -401,9 +405,8 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
     cudaError_t e = launch_pdl(k_gemm_tc<FMT, BN, E>, grid, dim3(kThreads), C::kSmem, s, a0, a1, b0,
                                b1, bias, M, N, K, ea, err, sk.splits, sk.part);
     if (e != cudaSuccess || sk.splits == 1) return e;
-    const size_t total = static_cast<size_t>(M) * N;
-    const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
-    return launch_pdl(k_splitk_reduce<E>, dim3(blocks), dim3(256), 0, s, sk.part, sk.splits, M, N,
+    const dim3 rgrid((N + 255) / 256, std::min(M, std::max(1, 148 * 8 / ((N + 255) / 256))));
+    return launch_pdl(k_splitk_reduce<E>, rgrid, dim3(256), 0, s, sk.part, sk.splits, M, N,
                       bias, ea);
 }
 
@@ -467,13 +470,12 @@ size_t tc_split_bytes(int M, int K, int w_bf16) {
 cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M, int K, int w_bf16,
                                  void* hi, void* lo) {
     if (M <= 0) return cudaSuccess;
-    const size_t total = static_cast<size_t>(M) * K;
-    const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 16));
+    const dim3 grid((K + 255) / 256, std::min(M, std::max(1, 148 * 16 / ((K + 255) / 256))));
     if (w_bf16) {
-        return launch_pdl(k_split_bf16, dim3(blocks), dim3(256), 0, s, x, ldx, M, K,
+        return launch_pdl(k_split_bf16, grid, dim3(256), 0, s, x, ldx, M, K,
                           static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
     }
-    return launch_pdl(k_split_tf32, dim3(blocks), dim3(256), 0, s, x, ldx, M, K,
+    return launch_pdl(k_split_tf32, grid, dim3(256), 0, s, x, ldx, M, K,
                       static_cast<float*>(hi), static_cast<float*>(lo));
 }
 

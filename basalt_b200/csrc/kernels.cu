@@ -406,7 +406,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
     const int* __restrict__ rowmap, const int* __restrict__ len, int heads, int slots,
     float scale, int splits, int chunk, float* __restrict__ part, int* __restrict__ tickets,
-    float* __restrict__ out) {
+    float* __restrict__ out, PlaneOut po) {
     constexpr int EPV = Vec16<KT>::N;
     constexpr int LPK = HD / EPV;  // lanes per key
     constexpr int KPW = 32 / LPK;  // keys per warp step
@@ -501,7 +501,9 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     if (splits == 1) {
         for (int e = tid; e < HD; e += 128) {
             const float acc = red[e] + red[HD + e] + red[2 * HD + e] + red[3 * HD + e];
-            out[static_cast<size_t>(i) * d + h * HD + e] = acc / sum;
+            const size_t at = static_cast<size_t>(i) * d + h * HD + e;
+            out[at] = acc / sum;
+            if (po.planes) store_split(acc / sum, po.planes, po.hi, po.lo, at);
         }
         return;
     }
@@ -531,7 +533,9 @@ __global__ __launch_bounds__(128) void k_attn_decode(
             L = fmaf(__ldcg(all + z * (HD + 2) + HD + 1), wgt, L);
             O = fmaf(__ldcg(all + z * (HD + 2) + e), wgt, O);
         }
-        out[static_cast<size_t>(i) * d + h * HD + e] = O / L;
+        const size_t at = static_cast<size_t>(i) * d + h * HD + e;
+        out[at] = O / L;
+        if (po.planes) store_split(O / L, po.planes, po.hi, po.lo, at);
     }
     if (tid == 0) tickets[i * heads + h] = 0;
 }
@@ -544,7 +548,8 @@ template <typename KT, int HD, int QPW>
 __global__ __launch_bounds__(128) void k_attn_prefill(
     const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
     const int* __restrict__ seg_row, const int* __restrict__ seg_start,
-    const int* __restrict__ seg_len, int heads, int slots, float scale, float* __restrict__ out) {
+    const int* __restrict__ seg_len, int heads, int slots, float scale, float* __restrict__ out,
+    PlaneOut po) {
     pdl_trigger();
     pdl_wait();
     constexpr int QT = 4 * QPW;
@@ -619,7 +624,9 @@ __global__ __launch_bounds__(128) void k_attn_prefill(
         if (t >= n) continue;
 #pragma unroll
         for (int c = 0; c < DPL; ++c) {
-            out[static_cast<size_t>(start + t) * d + h * HD + lane * DPL + c] = o[r][c] / l[r];
+            const size_t at = static_cast<size_t>(start + t) * d + h * HD + lane * DPL + c;
+            out[at] = o[r][c] / l[r];
+            if (po.planes) store_split(o[r][c] / l[r], po.planes, po.hi, po.lo, at);
         }
     }
 }
@@ -880,34 +887,35 @@ template <typename KT, int HD>
 cudaError_t attn_decode_typed(cudaStream_t s, const float* q, const void* kc, const void* vc,
                               const int* rowmap, const int* len, int R, int heads, int slots,
                               float scale, int splits, int chunk, float* part, int* tickets,
-                              float* out) {
+                              float* out, const PlaneOut& po) {
     return launch_pdl(k_attn_decode<KT, HD>, dim3(R * heads, splits), 128, 0, s, q,
                       static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len, heads,
-                      slots, scale, splits, chunk, part, tickets, out);
+                      slots, scale, splits, chunk, part, tickets, out, po);
 }
 
 template <typename KT, int HD>
 cudaError_t attn_prefill_typed(cudaStream_t s, const float* q, const void* kc, const void* vc,
                                const int* seg_row, const int* seg_start, const int* seg_len,
                                int segments, int max_len, int heads, int slots, float scale,
-                               float* out) {
+                               float* out, const PlaneOut& po) {
     constexpr int QPW = HD > 64 ? 4 : 8;
     const dim3 grid(segments, heads, (max_len + 4 * QPW - 1) / (4 * QPW));
-    return launch_pdl(k_attn_prefill<KT, HD, QPW>, grid, 128, 0, s, 
+    return launch_pdl(k_attn_prefill<KT, HD, QPW>, grid, 128, 0, s,
         q, static_cast<const KT*>(kc), static_cast<const KT*>(vc), seg_row, seg_start, seg_len,
-        heads, slots, scale, out);
+        heads, slots, scale, out, po);
 }
 }  // namespace
 
 cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
                                const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
                                int R, int heads, int head_dim, int slots, float scale, int splits,
-                               int chunk, float* part, int* tickets, float* out) {
+                               int chunk, float* part, int* tickets, float* out,
+                               const PlaneOut& planes) {
     if (R <= 0) return cudaSuccess;
     if (chunk > kMaxChunk) return cudaErrorInvalidValue;
 #define BST_ATTN_DEC(KT, HD)                                                                    \
     return attn_decode_typed<KT, HD>(s, q, k_cache, v_cache, rowmap, len, R, heads, slots,      \
-                                     scale, splits, chunk, part, tickets, out)
+                                     scale, splits, chunk, part, tickets, out, planes)
     if (kv_bf16) {
         switch (head_dim) {
             case 32: BST_ATTN_DEC(__nv_bfloat16, 32);
@@ -929,11 +937,11 @@ cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_ca
                                 const void* v_cache, int kv_bf16, const int* seg_row,
                                 const int* seg_start, const int* seg_len, int segments,
                                 int max_len, int heads, int head_dim, int slots, float scale,
-                                float* out) {
+                                float* out, const PlaneOut& planes) {
     if (segments <= 0) return cudaSuccess;
 #define BST_ATTN_PRE(KT, HD)                                                                    \
     return attn_prefill_typed<KT, HD>(s, q, k_cache, v_cache, seg_row, seg_start, seg_len,      \
-                                      segments, max_len, heads, slots, scale, out)
+                                      segments, max_len, heads, slots, scale, out, planes)
     if (kv_bf16) {
         switch (head_dim) {
             case 32: BST_ATTN_PRE(__nv_bfloat16, 32);

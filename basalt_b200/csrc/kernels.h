@@ -41,6 +41,16 @@ enum class Epi : int {
     kLogits = 5,       // out[rowmap[m], n] = value
 };
 
+// Optional second copy of an output as tensor-core operand planes ([rows][ld], see
+// launch_split_operand): the producer of a projection's input writes them so that the projection
+// needs no separate split pass.
+struct PlaneOut {
+    void* hi = nullptr;
+    void* lo = nullptr;
+    int planes = 0;  // 0 none, 1 tf32 hi + fp32 remainder, 2 two bf16 planes
+    int ld = 0;
+};
+
 struct EpiArgs {
     float* out = nullptr;
     int ldo = 0;
@@ -52,6 +62,7 @@ struct EpiArgs {
     void* v_cache = nullptr;
     int d = 0, heads = 0, head_dim = 0, slots = 0;
     int kv_bf16 = 0;
+    PlaneOut split;                // kStore, kGelu: also write the result as operand planes
 };
 
 // Optional LayerNorm applied to a projection's input rows (the pre-norm of TransformerBlock).
@@ -94,14 +105,15 @@ cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const floa
 cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
                                const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
                                int R, int heads, int head_dim, int slots, float scale, int splits,
-                               int chunk, float* part, int* tickets, float* out);
+                               int chunk, float* part, int* tickets, float* out,
+                               const PlaneOut& planes = PlaneOut{});
 // Causal prefill attention for `segments` rows; token t of segment j is packed at
 // seg_start[j] + t and sits in cache slot t of row seg_row[j].
 cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,
                                 const void* v_cache, int kv_bf16, const int* seg_row,
                                 const int* seg_start, const int* seg_len, int segments,
                                 int max_len, int heads, int head_dim, int slots, float scale,
-                                float* out);
+                                float* out, const PlaneOut& planes = PlaneOut{});
 
 // Prefill token list from the device windows: for segment j (row seg_row[j], npad leading PAD
 // ids), tokens window[row][npad + t] at positions t; a segment with no real token gets one PAD id
