@@ -472,9 +472,18 @@ class Engine {
                  double* scores, float* logits);
     void plan(const std::vector<int32_t>& windows, int rows, int steps,
               std::vector<StepPlan>* plans, int* max_slots, int* max_tokens) const;
+    // presplit: the operand planes are already in ws.ys_* (planes_for) or, with presplit_xs, in
+    // ws.xs_* (written by residual_ln).
     int linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N, int K,
                Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln = nullptr,
-               bool presplit = false);
+               bool presplit = false, bool presplit_xs = false);
+    // x += X W^T + bias (a residual projection) followed by the LayerNorm `next` of the new x.
+    // On the tensor-core path with a K split, one fused fix-up kernel does both and leaves the
+    // normalised rows as operand planes in ws.xs_* (*normalised = true); otherwise it runs the
+    // plain residual projection and the caller applies `next` itself.
+    int residual_ln(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N,
+                    int K, bool presplit, const bst::LnArgs& next, const char* what,
+                    bool* normalised);
     // Whether linear() takes the tensor-core path for this shape, and the operand planes a
     // producer should write for it (into ws.ys_*; none when the GEMV path consumes fp32).
     bool linear_on_tc(const Matrix& m, int M, int N, int K) const;
@@ -881,9 +890,49 @@ bst::PlaneOut Engine::planes_for(const Matrix& m, int M, int N, int K) const {
     return po;
 }
 
+int Engine::residual_ln(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N,
+                        int K, bool presplit, const bst::LnArgs& next, const char* what,
+                        bool* normalised) {
+    *normalised = false;
+    EpiArgs res;
+    res.out = ws.x;
+    res.ldo = d;
+    const int splits = linear_on_tc(m, M, N, K)
+                           ? bst::tc_plan(M, N, K, wbf16, bst::tc_part_bytes_max(), nullptr)
+                           : 1;
+    if (splits <= 1 || N > 1024 || N != d) {
+        return linear(x, ldx, m, bias, M, N, K, Epi::kResidual, res, what, nullptr, presplit);
+    }
+    const double plane = static_cast<double>(bst::tc_split_bytes(M, K, wbf16));
+    const double wbytes = static_cast<double>(N) * K * (wbf16 ? 2.0 : 8.0);
+    cudaError_t err;
+    if (!presplit) {
+        err = launch(bst::kSplit, M * K * 4.0 + 2 * plane, 0, 1, [&] {
+            return bst::launch_split_operand(stream, x, ldx, M, K, wbf16, ws.ys_hi, ws.ys_lo);
+        });
+        if (err) return cuda_fail(err, what);
+    }
+    err = launch(bst::kGemm, wbytes + 2 * plane + static_cast<double>(splits) * M * N * 4.0,
+                 2.0 * M * N * K, 1, [&] {
+                     return bst::launch_gemm_tc(stream, ws.ys_hi, ws.ys_lo, wbf16 ? m.w : m.hi,
+                                                m.lo, wbf16, bias, M, N, K, Epi::kResidual, res,
+                                                ws.err, ws.tc_part, bst::tc_part_bytes_max(),
+                                                true);
+                 });
+    if (err) return cuda_fail(err, what);
+    const double out_plane = static_cast<double>(bst::tc_split_bytes(M, N, wbf16));
+    err = launch(bst::kLayerNorm, (splits + 2.0) * M * N * 4.0 + 2 * out_plane, 0, 1, [&] {
+        return bst::launch_reduce_residual_ln(stream, ws.tc_part, splits, M, N, bias, ws.x, d, next,
+                                              ws.xs_hi, ws.xs_lo, wbf16 ? 2 : 1);
+    });
+    if (err) return cuda_fail(err, what);
+    *normalised = true;
+    return BST_OK;
+}
+
 int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, int M, int N,
                    int K, Epi epi, const EpiArgs& ea, const char* what, const bst::LnArgs* ln,
-                   bool presplit) {
+                   bool presplit, bool presplit_xs) {
     const double wb = wbf16 ? 2.0 : 4.0;
     cudaError_t err;
     if (linear_on_tc(m, M, N, K)) {
@@ -892,9 +941,9 @@ int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, 
         // pass.
         const double plane = static_cast<double>(bst::tc_split_bytes(M, K, wbf16));
         const int planes = wbf16 ? 2 : 1;
-        const void* a_hi = presplit ? ws.ys_hi : ws.xs_hi;
-        const void* a_lo = presplit ? ws.ys_lo : ws.xs_lo;
-        if (presplit) {
+        const void* a_hi = presplit && !presplit_xs ? ws.ys_hi : ws.xs_hi;
+        const void* a_lo = presplit && !presplit_xs ? ws.ys_lo : ws.xs_lo;
+        if (presplit || presplit_xs) {
             err = cudaSuccess;
         } else if (ln) {
             err = launch(bst::kLayerNorm, M * K * 4.0 + 2 * plane, 0, 1, [&] {
@@ -920,6 +969,7 @@ int Engine::linear(const float* x, int ldx, const Matrix& m, const float* bias, 
                      });
         return err ? cuda_fail(err, what) : BST_OK;
     }
+    if (presplit_xs) return fail(BST_PANIC, std::string(what) + ": operand planes on the GEMV path");
     const bst::LnArgs* fused = nullptr;
     if (ln) {
         if (bst::linear_fuses_layernorm(M, N, K)) {
@@ -1066,6 +1116,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
                                                        ws.next, ws.len, ws.slot, ws.x, R, d);
                    }), "embedding");
     if (st) return st;
+    bool x_normalised = false;  // ws.xs_* holds this layer's LN1 (or the final LN) of ws.x
     for (int l = 0; l < L; ++l) {
         const LayerWeights& lw = layers[l];
         const bst::LnArgs ln1{lw.ln1_g, lw.ln1_b, kLayerNormEps};
@@ -1081,7 +1132,10 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         qkv.head_dim = hd;
         qkv.slots = slots;
         qkv.kv_bf16 = kvbf16;
-        st = linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv, "qkv projection", &ln1);
+        st = x_normalised ? linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
+                                   "qkv projection", nullptr, false, true)
+                          : linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
+                                   "qkv projection", &ln1);
         if (st) return st;
         const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0;
         const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
@@ -1092,21 +1146,25 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
                                                       ws.attn_tickets, ws.att, att_planes);
                    }), "decode attention");
         if (st) return st;
-        EpiArgs res;
-        res.out = ws.x;
-        res.ldo = d;
-        st = linear(ws.att, d, lw.wo, lw.bo, R, d, d, Epi::kResidual, res, "output projection",
-                    nullptr, att_planes.planes != 0);
-        if (st) return st;
         const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
+        bool ffn_in_normalised = false;
+        st = residual_ln(ws.att, d, lw.wo, lw.bo, R, d, d, att_planes.planes != 0, ln2,
+                         "output projection", &ffn_in_normalised);
+        if (st) return st;
         EpiArgs act;
         act.out = ws.ffn;
         act.ldo = F;
         act.split = planes_for(lw.w2, R, d, F);
-        st = linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1", &ln2);
+        st = ffn_in_normalised ? linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
+                                        nullptr, false, true)
+                               : linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
+                                        &ln2);
         if (st) return st;
-        st = linear(ws.ffn, F, lw.w2, lw.b2, R, d, F, Epi::kResidual, res, "ffn2", nullptr,
-                    act.split.planes != 0);
+        const bst::LnArgs next = l + 1 < L ? bst::LnArgs{layers[l + 1].ln1_g, layers[l + 1].ln1_b,
+                                                         kLayerNormEps}
+                                           : bst::LnArgs{lnf_g, lnf_b, kLayerNormEps};
+        st = residual_ln(ws.ffn, F, lw.w2, lw.b2, R, d, F, act.split.planes != 0, next, "ffn2",
+                         &x_normalised);
         if (st) return st;
     }
     const bst::LnArgs lnf{lnf_g, lnf_b, kLayerNormEps};
@@ -1114,7 +1172,9 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = rowmap;
-    return linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head", &lnf);
+    return x_normalised ? linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head",
+                                 nullptr, false, true)
+                        : linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head", &lnf);
 }
 
 // Families without a cache: the whole window is the input every step.

@@ -152,7 +152,8 @@ struct Config {
     static constexpr int kBytesA = kTileRowsA * kRowBytes;  // one plane
     static constexpr int kBytesB = BN * kRowBytes;
     static constexpr int kStageBytes = kPlanesA * kBytesA + kPlanesB * kBytesB;
-    static constexpr int kStages = (192 * 1024) / kStageBytes;
+    // Narrow tiles serve the short decode GEMMs: two stages (<= 96 KB) let two CTAs share an SM.
+    static constexpr int kStages = BN == 64 ? 2 : (192 * 1024) / kStageBytes;
     static constexpr int kElemsPerRow = FMT == 2 ? 32 : 64;  // K per stage
     static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
     static constexpr int kTmemCols = BN < 32 ? 32 : BN;
@@ -394,6 +395,7 @@ cudaError_t make_map(CUtensorMap* map, const void* ptr, int rows, int K, bool bf
 struct SplitK {
     int splits = 1;
     float* part = nullptr;
+    bool defer = false;  // leave the split sums to the caller (launch_reduce_residual_ln)
 };
 
 template <int FMT, int BN, Epi E>
@@ -404,7 +406,7 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
     const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits);
     cudaError_t e = launch_pdl(k_gemm_tc<FMT, BN, E>, grid, dim3(kThreads), C::kSmem, s, a0, a1, b0,
                                b1, bias, M, N, K, ea, err, sk.splits, sk.part);
-    if (e != cudaSuccess || sk.splits == 1) return e;
+    if (e != cudaSuccess || sk.splits == 1 || sk.defer) return e;
     const dim3 rgrid((N + 255) / 256, std::min(M, std::max(1, 148 * 8 / ((N + 255) / 256))));
     return launch_pdl(k_splitk_reduce<E>, rgrid, dim3(256), 0, s, sk.part, sk.splits, M, N,
                       bias, ea);
@@ -509,7 +511,8 @@ size_t tc_part_bytes(int M, int N, int K, int w_bf16) {
 
 cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, const void* w,
                            const void* w_lo, int w_bf16, const float* bias, int M, int N, int K,
-                           Epi epi, const EpiArgs& ea, int* err, float* part, size_t part_bytes) {
+                           Epi epi, const EpiArgs& ea, int* err, float* part, size_t part_bytes,
+                           bool defer_fixup) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     cudaError_t e = encoder();
     if (e != cudaSuccess) return e;
@@ -517,6 +520,7 @@ cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, c
     SplitK sk;
     sk.splits = tc_plan(M, N, K, w_bf16, part ? part_bytes : 0, &bn);
     sk.part = part;
+    sk.defer = defer_fixup;
     CUtensorMap a0, a1, b0, b1;
     if ((e = make_map(&a0, x_hi, M, K, w_bf16, BM)) != cudaSuccess) return e;
     if ((e = make_map(&a1, x_lo, M, K, w_bf16, BM)) != cudaSuccess) return e;

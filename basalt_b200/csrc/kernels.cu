@@ -396,6 +396,101 @@ __global__ __launch_bounds__(256) void k_layernorm(const float* __restrict__ x, 
     }
 }
 
+// Split-K fix-up of a residual projection, then the LayerNorm of the updated rows into operand
+// planes (see launch_reduce_residual_ln). One CTA of 128 threads per row; a thread owns EPT
+// columns (n = tid + 128 j) and loads their partials of up to 8 splits at once. The splits are
+// summed in order as k_splitk_reduce does; the f64 statistics are k_layernorm's up to the order
+// of the f64 additions.
+template <int EPT>
+__global__ __launch_bounds__(128) void k_reduce_residual_ln(
+    const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
+    float* __restrict__ x, int ldx, const float* __restrict__ gamma, const float* __restrict__ beta,
+    float eps, void* __restrict__ hi, void* __restrict__ lo, int planes) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int ZB = 8;
+    __shared__ double red[4];
+    __shared__ double stat;
+    const int m = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t total = static_cast<size_t>(M) * N;
+    float* xr = x + static_cast<size_t>(m) * ldx;
+    const float* pr = part + static_cast<size_t>(m) * N;
+    float v[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) v[j] = 0.0f;
+    for (int z0 = 0; z0 < splits; z0 += ZB) {
+        float t[EPT][ZB];
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+            const int n = min(tid + 128 * j, N - 1);
+#pragma unroll
+            for (int z = 0; z < ZB; ++z) {
+                t[j][z] = z0 + z < splits ? pr[static_cast<size_t>(z0 + z) * total + n] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+#pragma unroll
+            for (int z = 0; z < ZB; ++z) {
+                if (z0 + z < splits) v[j] += t[j][z];
+            }
+        }
+    }
+    // v = sum of splits; the residual add in the order of the kResidual epilogue
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        if (n < N) {
+            const float value = bias ? __fadd_rn(v[j], bias[n]) : v[j];
+            v[j] = __fadd_rn(xr[n], value);
+            xr[n] = v[j];
+        }
+    }
+    // f64 statistics over the row: per-thread partial sums, then the block
+    double s = 0.0;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        if (tid + 128 * j < N) s = __dadd_rn(s, static_cast<double>(v[j]));
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (tid == 0) stat = __ddiv_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])),
+                                   static_cast<double>(N));
+    __syncthreads();
+    const double mean = stat;
+    double q = 0.0;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        if (tid + 128 * j < N) {
+            const double delta = __dadd_rn(static_cast<double>(v[j]), -mean);
+            q = __dadd_rn(q, __dmul_rn(delta, delta));
+        }
+    }
+    q = warp_sum_d(q);
+    __syncthreads();
+    if (lane == 0) red[warp] = q;
+    __syncthreads();
+    if (tid == 0) {
+        const double variance = __ddiv_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])),
+                                          static_cast<double>(N));
+        stat = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(eps))));
+    }
+    __syncthreads();
+    const double inverse = stat;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        if (n < N) {
+            const float normalized =
+                static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(v[j]), -mean), inverse));
+            const float out = __fadd_rn(__fmul_rn(normalized, gamma[n]), beta[n]);
+            store_split(out, planes, hi, lo, static_cast<size_t>(m) * N + n);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Decode attention, split over the cached keys. One CTA per (row, head, split); writes the
 // split's running max, sum of exponentials and unnormalised output. Scores follow
@@ -905,6 +1000,20 @@ cudaError_t attn_prefill_typed(cudaStream_t s, const float* q, const void* kc, c
         heads, slots, scale, out, po);
 }
 }  // namespace
+
+cudaError_t launch_reduce_residual_ln(cudaStream_t s, const float* part, int splits, int M, int N,
+                                      const float* bias, float* x, int ldx, const LnArgs& ln,
+                                      void* hi, void* lo, int planes) {
+    if (M <= 0) return cudaSuccess;
+#define BST_RRL(EPT)                                                                             \
+    return launch_pdl(k_reduce_residual_ln<EPT>, dim3(M), 128, 0, s, part, splits, M, N, bias, x, \
+                      ldx, ln.gamma, ln.beta, ln.eps, hi, lo, planes)
+    if (N <= 256) BST_RRL(2);
+    if (N <= 512) BST_RRL(4);
+    if (N <= 1024) BST_RRL(8);
+#undef BST_RRL
+    return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
                                const void* v_cache, int kv_bf16, const int* rowmap, const int* len,

@@ -168,7 +168,14 @@ cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M,
 cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, const void* w,
                            const void* w_lo, int w_bf16, const float* bias, int M, int N, int K,
                            Epi epi, const EpiArgs& ea, int* err, float* part = nullptr,
-                           size_t part_bytes = 0);
+                           size_t part_bytes = 0, bool defer_fixup = false);
+// Fix-up of a split residual projection fused with the LayerNorm that follows it, one warp per
+// row: x[m, :] += sum_z part[z][m, :] + bias (splits in order, as the separate fix-up does), then
+// LayerNorm of the new row (f64 statistics) written as the next projection's operand planes.
+// N <= 1024.
+cudaError_t launch_reduce_residual_ln(cudaStream_t s, const float* part, int splits, int M, int N,
+                                      const float* bias, float* x, int ldx, const LnArgs& ln,
+                                      void* hi, void* lo, int planes);
 // Split count and tile width launch_gemm_tc chooses for this shape and scratch.
 int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out);
 // Partial scratch that lets every shape reach one full wave of CTAs, and what one shape needs.
