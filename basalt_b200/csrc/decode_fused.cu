@@ -340,12 +340,77 @@ __device__ __forceinline__ void store_out(Epi epi, const EpiArgs& ea, const Sink
     }
 }
 
+// LayerNorm statistics without a block-wide pass: each residual phase publishes, per row, the sum
+// and the centred sum of squares (M2) of the columns its CTA owns (f64); the next LayerNorm phase
+// combines the per-CTA pairs in CTA order with Chan's formula, M2 = sum_c [M2_c + n_c (mean_c -
+// mean)^2], which equals the two-pass statistics of nn_ops.rs:168-199 up to f64 rounding.
+// stats layout: [row][cta][2].
+__device__ __forceinline__ void publish_stats(const float* xown, int own_ld, int ncols, int R,
+                                              double* stats) {
+    if (threadIdx.x < R && ncols > 0) {
+        const int i = threadIdx.x;
+        const float* xr = xown + i * own_ld;
+        double s = 0.0;
+        for (int j = 0; j < ncols; ++j) s = __dadd_rn(s, static_cast<double>(xr[j]));
+        const double mc = __ddiv_rn(s, static_cast<double>(ncols));
+        double m2 = 0.0;
+        for (int j = 0; j < ncols; ++j) {
+            const double delta = __dadd_rn(static_cast<double>(xr[j]), -mc);
+            m2 = __dadd_rn(m2, __dmul_rn(delta, delta));
+        }
+        double* out = stats + (static_cast<size_t>(i) * gridDim.x + blockIdx.x) * 2;
+        out[0] = s;
+        out[1] = m2;
+    }
+}
+
+// Mean and 1/sqrt(var + eps) of R rows of width d from the published per-CTA statistics; warp i
+// handles row i. Results in mean[i], inv[i] (shared) after the caller's __syncthreads().
+__device__ __forceinline__ void combine_stats(const double* stats, int R, int d, float eps,
+                                              double* mean, double* inv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp >= R) return;
+    const int G = gridDim.x;
+    const int cpc = (d + G - 1) / G;
+    const double* rs = stats + static_cast<size_t>(warp) * G * 2;
+    constexpr int kPer = 8;  // CTAs per lane (grids up to 256)
+    double sc[kPer], m2c[kPer];
+    int nc[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int c = lane + 32 * k;
+        const int c0 = min(d, c * cpc);
+        nc[k] = c < G ? min(d, c0 + cpc) - c0 : 0;
+        sc[k] = nc[k] > 0 ? __ldcg(rs + 2 * c) : 0.0;
+        m2c[k] = nc[k] > 0 ? __ldcg(rs + 2 * c + 1) : 0.0;
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) s = __dadd_rn(s, sc[k]);
+    const double mu = __ddiv_rn(warp_sum_d(s), static_cast<double>(d));
+    double m2 = 0.0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        if (nc[k] > 0) {
+            const double delta = __dadd_rn(__ddiv_rn(sc[k], static_cast<double>(nc[k])), -mu);
+            m2 = __dadd_rn(m2, __dadd_rn(m2c[k], __dmul_rn(static_cast<double>(nc[k]), __dmul_rn(delta, delta))));
+        }
+    }
+    m2 = warp_sum_d(m2);
+    if (lane == 0) {
+        const double variance = __ddiv_rn(m2, static_cast<double>(d));
+        mean[warp] = mu;
+        inv[warp] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(eps))));
+    }
+}
+
 // Per-CTA state shared by the projection phases.
 struct Ctx {
     float* xs;    // [R][max(d, F)] projection input (shared)
     float* xraw;  // [R][d] rows before LayerNorm (shared)
     int R;
     float eps;
+    const double* stats;  // published per-CTA statistics of the input rows (LayerNorm phases)
 };
 
 // Y[R, N] = X[R, K] * W[N, K]^T + bias over the whole grid with the weights staged by
@@ -353,9 +418,9 @@ struct Ctx {
 // layer-normalised first when `ln`. Partial sums are combined in a fixed order, so results repeat
 // bit for bit.
 template <typename WT, int RT>
-__device__ __forceinline__ void gemv(const float* x, int ldx, bool staged, bool ln, const void* wv,
-                                  bool has_bias, int N, int K, Epi epi, const EpiArgs& ea,
-                                  const Sink& sk, const Ctx& cx, WStage& st) {
+__device__ __forceinline__ void gemv(const float* x, int ldx, bool staged, bool ln, bool use_stats,
+                                  const void* wv, bool has_bias, int N, int K, Epi epi,
+                                  const EpiArgs& ea, const Sink& sk, const Ctx& cx, WStage& st) {
     constexpr int VEC = Unpack<WT>::N;
     __shared__ float red[kWarps][RT];
     const int R = cx.R;
@@ -363,12 +428,24 @@ __device__ __forceinline__ void gemv(const float* x, int ldx, bool staged, bool 
     const int nvec = K / VEC;
     const Plan pl = make_plan(N, nvec);
     if (pl.c1 <= pl.c0) return;  // uniform over the CTA
-    if (ln) {
+    if (ln && use_stats) {
+        __shared__ double s_mean[RT], s_inv[RT];
+        stage_rows(x, ldx, R, K, cx.xraw);
+        combine_stats(cx.stats, R, K, cx.eps, s_mean, s_inv);
+        stage_wait(st);
+        __syncthreads();
+        for (int e = threadIdx.x; e < R * K; e += kThreads) {
+            const int i = e / K, k = e - i * K;
+            const float nrm = static_cast<float>(
+                __dmul_rn(__dadd_rn(static_cast<double>(cx.xraw[e]), -s_mean[i]), s_inv[i]));
+            xs[e] = __fadd_rn(__fmul_rn(nrm, st.lnp[k]), st.lnp[K + k]);
+        }
+    } else if (ln) {
         if (!staged) stage_rows(x, ldx, R, K, cx.xraw);
         stage_wait(st);
         __syncthreads();
         const LnArgs lns{st.lnp, st.lnp + K, cx.eps};
-        layernorm_rows(cx.xraw, K, RT == 1 ? 1 : R, K, lns, xs, true);
+        layernorm_rows(cx.xraw, K, RT == 1 ? 1 : R, K, lns, xs);
     } else {
         stage_rows(x, ldx, R, K, xs);
         stage_wait(st);
@@ -697,7 +774,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
     }
     GridSync gsync{p.bar, p.bar_base, p.err, &abort_flag};
     WStage st{&s_wbar, wbuf, p.wstage_bytes, bsm, lnp, &abort_flag, p.err, 0u, 0, 0, false};
-    const Ctx cx{xs, xraw, R, p.eps};
+    const Ctx cx{xs, xraw, R, p.eps, p.stats};
     __syncthreads();
     {
         const ProjDesc pd = describe(p, lt, 0);
@@ -747,8 +824,14 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
             ea.head_dim = hd;
             ea.slots = p.slots;
             ea.kv_bf16 = sizeof(KT) == 2;
-            gemv<WT, RT>(pd.x, pd.ldx, phase == 0, pd.ln_g != nullptr, pd.w, pd.bias != nullptr,
-                         pd.N, pd.K, pd.epi, ea, sk, cx, st);
+            // LayerNorm inputs after a residual phase use its published statistics; layer 0's
+            // input comes from the embedding every CTA computed itself.
+            gemv<WT, RT>(pd.x, pd.ldx, phase == 0, pd.ln_g != nullptr, phase > 0, pd.w,
+                         pd.bias != nullptr, pd.N, pd.K, pd.epi, ea, sk, cx, st);
+            if (kind == 2 || kind == 4) {
+                __syncthreads();
+                publish_stats(xown, own_ld, dc1 - dc0, R, p.stats);
+            }
         }
         if (phase == last) break;
         if (kind != 0) {  // the next phase is a projection: stage its weights before the barrier
@@ -844,7 +927,7 @@ int prepare_typed(int R, int d, int F, int V, int L) {
         return 0;
     }
     const Layout lay = fused_layout(R, d, F, V, L, sms);
-    if (!coop || !lay.ok) return 0;
+    if (!coop || !lay.ok || sms > 256) return 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemLimit)) != cudaSuccess) {
         cudaGetLastError();

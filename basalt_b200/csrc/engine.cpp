@@ -319,6 +319,7 @@ struct Workspace {
     float* tc_part = nullptr;                 // split-K partial products
     unsigned* bar = nullptr;                  // fused decode step: barrier count, head ticket
     unsigned long long* best = nullptr;       // fused decode step: per-row packed maximum [8]
+    double* fused_stats = nullptr;            // fused decode step: LayerNorm statistics [8][256][2]
     bst::FusedLayer* fused_layers = nullptr;  // fused decode step: per-layer table [L]
     void *k_cache = nullptr, *v_cache = nullptr;
     size_t kv_layer_elems = 0;
@@ -745,6 +746,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     add(reinterpret_cast<void**>(&ws.err), sizeof(int));
     add(reinterpret_cast<void**>(&ws.bar), 2 * sizeof(unsigned));
     add(reinterpret_cast<void**>(&ws.best), 8 * sizeof(unsigned long long));
+    add(reinterpret_cast<void**>(&ws.fused_stats), 8 * 256 * 2 * sizeof(double));
     {
         // Split planes for the widest tensor-core operand this run can see.
         const int kmax = decoder_family(spec.family) ? std::max(d, F)
@@ -1298,6 +1300,7 @@ int Engine::enqueue_fused(int rows, int steps, const std::vector<int>& lens, boo
     p.bar_base = fused_bar_base;
     p.best = ws.best;
     p.err = ws.err;
+    p.stats = ws.fused_stats;
     p.history = history ? ws.history : nullptr;
     if (p.nchunks > ws.splits) return fail(BST_PANIC, "decode chunk count exceeds the workspace");
     // Algorithmic bytes: every weight once, the cache rows attended, activations are negligible.

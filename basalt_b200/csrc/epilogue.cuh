@@ -75,13 +75,13 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float
 
 // Block-level LayerNorm of `rows` rows of x into out ([rows][d], shared memory), with the
 // statistics of nn_ops.rs:168-199 (f64 mean and population variance, f32 affine). One row uses
-// every warp of the block unless `warp_rows` is set; several rows take one warp each.
+// every warp of the block; several rows take one warp each.
 __device__ __forceinline__ void layernorm_rows(const float* __restrict__ x, int ldx, int rows, int d,
-                               const LnArgs& ln, float* __restrict__ out, bool warp_rows = false) {
+                               const LnArgs& ln, float* __restrict__ out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ double red[32];
     __shared__ double s_stat[2];
-    if (rows == 1 && !warp_rows) {
+    if (rows == 1) {
         const int nwarps = static_cast<int>(blockDim.x >> 5);
         double s = 0.0;
         for (int k = threadIdx.x; k < d; k += blockDim.x) s = __dadd_rn(s, static_cast<double>(x[k]));

@@ -221,6 +221,7 @@ struct FusedStep {
     unsigned bar_base = 0;         // bar[0] when this launch starts
     unsigned long long* best = nullptr;  // [R] packed per-row maximum, zero between launches
     int* err = nullptr;            // non-zero when a grid barrier timed out
+    double* stats = nullptr;       // [R][grid][2] per-CTA LayerNorm statistics (grid <= 256)
     float* history = nullptr;      // optional [R, steps, V] logits
     unsigned table_offset = 0;                     // layer table in shared memory (set by launch)
     unsigned wstage_offset = 0, wstage_bytes = 0;  // weight stage in shared memory (set by launch)
