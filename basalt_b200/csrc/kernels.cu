@@ -524,8 +524,9 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __syncthreads();
     const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
     const int sub = lane % LPK, kk = lane / LPK;
-    // Scores: U key groups per round, their 16-byte loads all in flight before any is used.
-    constexpr int U = 4;
+    // Scores: U key groups per round, their 16-byte loads all in flight before any is used
+    // (32 floats per lane).
+    constexpr int U = 32 / EPV;
     for (int j0 = warp * KPW; j0 < n; j0 += 4 * KPW * U) {
         float kv[U][EPV];
 #pragma unroll
@@ -568,8 +569,8 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __syncthreads();
     sum = stat[4] + stat[5] + stat[6] + stat[7];
     // Weighted values: each warp takes every 4th key, UV keys per round with their loads issued
-    // before the multiply-adds.
-    constexpr int UV = 8;
+    // before the multiply-adds (up to 32 floats per lane).
+    constexpr int UV = 32 / DPL < 16 ? 32 / DPL : 16;
     float o[DPL];
 #pragma unroll
     for (int c = 0; c < DPL; ++c) o[c] = 0.0f;
