@@ -7,7 +7,7 @@
 // by a grid barrier. Every projection spreads its weight rows over all SMs, so each weight byte is
 // read once per step with the whole chip's memory parallelism. Weights are constant during the
 // step: before the grid barrier that precedes a projection, each CTA has the TMA unit copy its
-// block of weight rows into shared memory (cp.async.bulk, no multicast), so the weight stream
+// block of weight rows into shared memory (cp.async.bulk into this CTA only), so the weight stream
 // overlaps the barrier and the input staging.
 //
 // Phases (R <= 8 rows, every row extending its cache; TransformerBlock.forward,
@@ -205,7 +205,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// One contiguous global -> shared copy by the TMA unit (no multicast), completing on `bar`.
+// One contiguous global -> shared copy by the TMA unit into this CTA, completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

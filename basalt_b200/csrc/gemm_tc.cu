@@ -1,5 +1,5 @@
 // Tensor-core projections for M > 8 rows on sm_100a: tcgen05.mma with accumulators in TMEM,
-// operands staged in shared memory by TMA (cp.async.bulk.tensor, no multicast).
+// operands staged in shared memory by TMA (cp.async.bulk.tensor, one CTA per copy).
 //
 // Y[M, N] = X[M, K] * W[N, K]^T + bias, epilogue fused (see Epi).
 //
