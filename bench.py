@@ -206,20 +206,34 @@ def batch1(local, steps, warmup):
     per_token_ms = (full_ms - prefill_ms) / (w.steps - 1)
     prof, kernels = profile_summary(engine, lambda: call(w.steps, d_tok))
     hbm, _, src = measured_peaks()
-    gemv = prof.get("gemv")
-    gemv_gbs = gemv["bytes"] / (gemv["ms"] / 1000.0) / 1e9 if gemv and gemv["ms"] else None
-    attn = prof.get("attn_decode")
-    attn_gbs = attn["bytes"] / (attn["ms"] / 1000.0) / 1e9 if attn and attn["ms"] else None
-    step = prof.get("decode_step")
-    step_gbs = step["bytes"] / (step["ms"] / 1000.0) / 1e9 if step and step["ms"] else None
+
+    def gbs(entry):
+        return entry["bytes"] / (entry["ms"] / 1000.0) / 1e9 if entry and entry["ms"] else None
+
+    step_gbs = gbs(prof.get("decode_step"))
+    # The same decode on the kernel-per-operation path (the fused step switched off), for the
+    # GEMV and attention kernels' own bandwidth.
+    os.environ["BST_FUSED_DECODE"] = "0"
+    try:
+        unfused_ms = timed(w.steps, d_tok, max(1, steps // 2))
+        uprof, ukernels = profile_summary(engine, lambda: call(w.steps, d_tok))
+    finally:
+        del os.environ["BST_FUSED_DECODE"]
+    gemv_gbs = gbs(uprof.get("gemv"))
+    attn_gbs = gbs(uprof.get("attn_decode"))
     engine.close()
     return {"workload": w.name, "tokens_per_s": w.steps / (full_ms / 1000.0),
             "ms_per_call": full_ms, "prefill_ms": prefill_ms,
             "decode_ms_per_token": per_token_ms,
-            "gemv_GBps": gemv_gbs, "gemv_frac": gemv_gbs / hbm if gemv_gbs else None,
-            "attn_decode_GBps": attn_gbs,
             "decode_step_GBps": step_gbs, "decode_step_frac": step_gbs / hbm if step_gbs else None,
-            "peak_source": src, "kernels": kernels}
+            "kernels": kernels,
+            "per_operation_path": {
+                "decode_ms_per_token": (unfused_ms - prefill_ms) / (w.steps - 1),
+                "gemv_GBps": gemv_gbs, "gemv_frac": gemv_gbs / hbm if gemv_gbs else None,
+                "attn_decode_GBps": attn_gbs,
+                "attn_decode_frac": attn_gbs / hbm if attn_gbs else None,
+                "kernels": ukernels},
+            "peak_source": src}
 
 
 def run_reference(args, rank, world):
@@ -383,6 +397,19 @@ def main():
     step_ms = ms / args.steps
     decode_tps = R * (steps - 1) / max(1e-9, (step_ms - prefill_ms) / 1000.0)
 
+    # The decode step as a whole against HBM: every weight once plus the K/V every row reads
+    # (mean cache length over the call), per decode step.
+    kvb = 2 if m.kv_dtype == "bf16" else 4
+    wbytes = 2 if m.weight_dtype == "bf16" else 4
+    params = m.layers * (4 * m.dimension ** 2 + 2 * m.dimension * m.hidden) + m.vocabulary * m.dimension
+    mean_len = min(m.window, workload.prompt + (steps + 1) / 2.0)
+    step_bytes = R * m.layers * 2 * m.dimension * kvb * mean_len + params * wbytes
+    step_s = max(1e-12, (step_ms - prefill_ms) / 1000.0 / max(1, steps - 1))
+    hbm_peak, _, _ = measured_peaks()
+    step_hbm = {"achieved": step_bytes / step_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                "frac": step_bytes / step_s / 1e9 / hbm_peak, "bytes_per_step": step_bytes,
+                "mean_cache_len": mean_len}
+
     # Per-kernel device time with CUDA events around each launch (one instrumented step).
     prof, kernels = profile_summary(engine, device_step)
     top = max(prof.items(), key=lambda kv: kv[1]["ms"])
@@ -391,9 +418,14 @@ def main():
     per_launch_s = k["ms"] / 1000.0 / k["launches"]
     if name in ("gemm",):
         achieved = k["flops"] / k["launches"] / per_launch_s / 1e12
+        # fp32 weights run as 3xTF32 (three tf32 passes, tf32 at half the bf16 rate); bf16
+        # weights as two bf16 passes: the ceiling for useful flops is the bf16 peak over that.
+        passes, rate = (2, 1.0) if m.weight_dtype == "bf16" else (3, 0.5)
+        useful_peak = bf16 * rate / passes
         roofline = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
                     "frac": achieved / bf16, "traffic": None, "kernel": name,
-                    "peak_source": peak_src}
+                    "peak_source": peak_src, "tensor_passes": passes,
+                    "useful_flops_peak": useful_peak, "useful_frac": achieved / useful_peak}
     else:
         achieved = k["bytes"] / k["launches"] / per_launch_s / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -414,6 +446,7 @@ def main():
                    "weights": m.weight_dtype, "kv_cache": m.kv_dtype,
                    "l2": "inputs larger than L2 (KV cache > 1 GB per GPU)"},
         "prefill_ms": prefill_ms, "decode_tokens_per_s": decode_tps * world,
+        "decode_step_hbm": step_hbm,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(ctx.nbytes), "d2h_bytes_per_step": int(R * steps * 4)},
         "gpu_launches": int(launches),
