@@ -315,6 +315,9 @@ struct Workspace {
     bool has_history = false;
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
     void *ys_hi = nullptr, *ys_lo = nullptr;  // planes a producer writes for the next projection
+    // The second decode lane's operand planes ([rows][max(d, F)]) and split-K partials.
+    void *lane_xs_hi = nullptr, *lane_xs_lo = nullptr, *lane_ys_hi = nullptr, *lane_ys_lo = nullptr;
+    float* lane_part = nullptr;
     int* err = nullptr;                       // tensor-core pipeline error code
     float* tc_part = nullptr;                 // split-K partial products
     unsigned* bar = nullptr;                  // fused decode step: barrier count, head ticket
@@ -344,6 +347,10 @@ class Engine {
     bst_model_spec spec{};
     int device = 0;
     cudaStream_t stream = nullptr;
+    // Second lane of the batched decode step: half of the rows run their layers on stream2 (forked
+    // from and joined back into `stream`), so one half's attention overlaps the other's GEMMs.
+    cudaStream_t stream2 = nullptr;
+    cudaEvent_t lane_fork = nullptr, lane_join = nullptr;
     int V = 0, W = 0, d = 0, L = 0, H = 0, hd = 0, F = 0;
     bool wbf16 = false, kvbf16 = false;
     std::vector<std::string> names;
@@ -413,6 +420,11 @@ class Engine {
         event_pool.clear();
         if (stream) cudaStreamDestroy(stream);
         stream = nullptr;
+        if (stream2) cudaStreamDestroy(stream2);
+        stream2 = nullptr;
+        if (lane_fork) cudaEventDestroy(lane_fork);
+        if (lane_join) cudaEventDestroy(lane_join);
+        lane_fork = lane_join = nullptr;
     }
 
     // ---- launches with optional per-class timing ----
@@ -491,6 +503,9 @@ class Engine {
     bst::PlaneOut planes_for(const Matrix& m, int M, int N, int K) const;
     int enqueue_prefill(const StepPlan& p, size_t begin, size_t end);
     int enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens);
+    // The layers and head of a decode step for R rows whose embedded inputs are in ws.x, on
+    // `stream` (enqueue_decode runs it once, or once per lane with the workspace views shifted).
+    int decode_layers(int R, const int* rowmap, const std::vector<int>& lens);
     int enqueue_direct(int rows);
     int prepare_fused(int rows);
     int enqueue_fused(int rows, int steps, const std::vector<int>& lens, bool history);
@@ -756,6 +771,14 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
         add(&ws.xs_lo, plane);
         add(&ws.ys_hi, plane);
         add(&ws.ys_lo, plane);
+        if (decoder_family(spec.family)) {
+            const size_t lane_plane = bst::tc_split_bytes(rows, std::max(d, F), wbf16);
+            add(&ws.lane_xs_hi, lane_plane);
+            add(&ws.lane_xs_lo, lane_plane);
+            add(&ws.lane_ys_hi, lane_plane);
+            add(&ws.lane_ys_lo, lane_plane);
+            add(reinterpret_cast<void**>(&ws.lane_part), bst::tc_part_bytes_max());
+        }
         add(reinterpret_cast<void**>(&ws.tc_part), bst::tc_part_bytes_max());
     }
     add(reinterpret_cast<void**>(&ws.rng), sizeof(uint64_t) * rows);
@@ -1097,7 +1120,53 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
 }
 
 int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens) {
-    const double wb = wbf16 ? 2.0 : 4.0, kvb = kvbf16 ? 2.0 : 4.0;
+    const double wb = wbf16 ? 2.0 : 4.0;
+    auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
+    int st = check(launch(bst::kEmbed, R * d * (2 * wb + 4.0), 0, 1, [&] {
+                       return bst::launch_embed_decode(stream, tok_emb, pos_emb, wbf16, rowmap,
+                                                       ws.next, ws.len, ws.slot, ws.x, R, d);
+                   }), "embedding");
+    if (st) return st;
+    const int RA = R / 2;
+    const bool lanes = stream2 && ws.lane_part && RA > 8 && R - RA <= ws.rows &&
+                       linear_on_tc(layers[0].wqkv, RA, 3 * d, d) &&
+                       linear_on_tc(layers[0].wqkv, R - RA, 3 * d, d);
+    if (!lanes) return decode_layers(R, rowmap, lens);
+    // Two lanes: rows [0, RA) on `stream`, rows [RA, R) on stream2 with every per-row workspace
+    // view shifted by RA rows and private planes and partials. Both start together; their
+    // kernels fill each other's idle SM time (starting the second lane a layer phase later, so
+    // that attention meets the other lane's projections, measured slower).
+    cudaError_t err = cudaEventRecord(lane_fork, stream);
+    if (!err) err = cudaStreamWaitEvent(stream2, lane_fork, 0);
+    if (err) return cuda_fail(err, "forking the decode lanes");
+    st = decode_layers(RA, rowmap, std::vector<int>(lens.begin(), lens.begin() + RA));
+    if (st) return st;
+    const Workspace saved = ws;
+    cudaStream_t main = stream;
+    stream = stream2;
+    ws.x += static_cast<size_t>(RA) * d;
+    ws.q += static_cast<size_t>(RA) * d;
+    ws.att += static_cast<size_t>(RA) * d;
+    ws.ffn += static_cast<size_t>(RA) * F;
+    ws.slot += RA;
+    ws.attn_tickets += static_cast<size_t>(RA) * H;
+    ws.part += static_cast<size_t>(RA) * H * ws.splits * (hd + 2);
+    ws.xs_hi = ws.lane_xs_hi;
+    ws.xs_lo = ws.lane_xs_lo;
+    ws.ys_hi = ws.lane_ys_hi;
+    ws.ys_lo = ws.lane_ys_lo;
+    ws.tc_part = ws.lane_part;
+    st = decode_layers(R - RA, rowmap + RA, std::vector<int>(lens.begin() + RA, lens.end()));
+    ws = saved;
+    stream = main;
+    if (st) return st;
+    err = cudaEventRecord(lane_join, stream2);
+    if (!err) err = cudaStreamWaitEvent(stream, lane_join, 0);
+    return err ? cuda_fail(err, "joining the decode lanes") : BST_OK;
+}
+
+int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens) {
+    const double kvb = kvbf16 ? 2.0 : 4.0;
     const int slots = ws.slots;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
     // Splits over the cache: enough CTAs for two waves of the SMs, chunks of >= 32 keys. Sized
@@ -1113,11 +1182,7 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     splits = (max_len + chunk - 1) / chunk;
     if (splits > ws.splits) return fail(BST_PANIC, "decode split count exceeds the workspace");
     auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
-    int st = check(launch(bst::kEmbed, R * d * (2 * wb + 4.0), 0, 1, [&] {
-                       return bst::launch_embed_decode(stream, tok_emb, pos_emb, wbf16, rowmap,
-                                                       ws.next, ws.len, ws.slot, ws.x, R, d);
-                   }), "embedding");
-    if (st) return st;
+    int st = BST_OK;
     bool x_normalised = false;  // ws.xs_* holds this layer's LN1 (or the final LN) of ws.x
     for (int l = 0; l < L; ++l) {
         const LayerWeights& lw = layers[l];
@@ -1684,6 +1749,9 @@ int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine
         }
         err = cudaSetDevice(device);
         if (!err) err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+        if (!err) err = cudaStreamCreateWithFlags(&e->stream2, cudaStreamNonBlocking);
+        if (!err) err = cudaEventCreateWithFlags(&e->lane_fork, cudaEventDisableTiming);
+        if (!err) err = cudaEventCreateWithFlags(&e->lane_join, cudaEventDisableTiming);
         if (!err) err = bst::configure_device_kernels_once(device);
         if (err) {
             cudaGetLastError();
