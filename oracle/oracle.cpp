@@ -961,6 +961,130 @@ extern "C" int32_t orc_generate_batch(orc_engine* e, const int32_t* contexts, in
     return 0;
 }
 
+// Greedy batch decode of the padded decoder with a per-row KV cache: the CPU engine a cached
+// implementation would be, for timing beside the full-window recompute above (which is what
+// TextEngine does). Each row appends one token per step (TransformerBlock.forward,
+// TransformerBlock.java:37-43, restated for one query position over the cached keys) and
+// re-encodes its window token by token once the window no longer starts with PAD, as the
+// positions of every cached token shift then. Rows run in parallel. Matrix products are the same
+// gemm.rs restatement at one row, so logits agree with the recompute up to rounding order.
+namespace {
+struct RowCache {
+    std::vector<float> k, v;  // [layers][W][d]
+    int64_t len = 0;
+};
+
+// Appends token `id` at position `pos` to the row's cache and writes the next-token logits.
+void cached_step(orc_engine* e, RowCache& rc, float id, float pos, float* logits) {
+    const orc_spec& s = e->spec;
+    const int64_t W = s.window, d = s.dimension, H = s.heads, hd = d / H, F = s.hidden;
+    std::vector<float> x(d), pe(d), h(d), q(d), kk(d), vv(d), ctx(d), o(d), f(F), sc(W);
+    embedding(e, &id, 1, e->p("embedding.weight"), d, x.data());
+    embedding(e, &pos, 1, e->p("position.weight"), d, pe.data());
+    for (int64_t i = 0; i < d; ++i) x[i] = x[i] + pe[i];
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
+    const int64_t t = rc.len;
+    for (int64_t layer = 0; layer < s.layers; ++layer) {
+        const std::string pre = "layer" + std::to_string(layer) + ".";
+        layer_norm(x.data(), e->p(pre + "norm1.gamma").data(), e->p(pre + "norm1.beta").data(),
+                   h.data(), 1, d, kLayerNormEps);
+        linear(e, h.data(), 1, d, d, pre + "attention.query", q.data());
+        linear(e, h.data(), 1, d, d, pre + "attention.key", kk.data());
+        linear(e, h.data(), 1, d, d, pre + "attention.value", vv.data());
+        float* kc = rc.k.data() + layer * W * d;
+        float* vc = rc.v.data() + layer * W * d;
+        std::memcpy(kc + t * d, kk.data(), sizeof(float) * d);
+        std::memcpy(vc + t * d, vv.data(), sizeof(float) * d);
+        for (int64_t hh = 0; hh < H; ++hh) {
+            for (int64_t j = 0; j <= t; ++j) {
+                float dot = 0.0f;
+                for (int64_t e2 = 0; e2 < hd; ++e2) dot += q[hh * hd + e2] * kc[j * d + hh * hd + e2];
+                sc[j] = dot * scale;
+            }
+            softmax_rows(sc.data(), sc.data(), 1, t + 1);
+            for (int64_t e2 = 0; e2 < hd; ++e2) {
+                float acc = 0.0f;
+                for (int64_t j = 0; j <= t; ++j) acc += sc[j] * vc[j * d + hh * hd + e2];
+                ctx[hh * hd + e2] = acc;
+            }
+        }
+        linear(e, ctx.data(), 1, d, d, pre + "attention.output", o.data());
+        for (int64_t i = 0; i < d; ++i) x[i] = x[i] + o[i];
+        layer_norm(x.data(), e->p(pre + "norm2.gamma").data(), e->p(pre + "norm2.beta").data(),
+                   h.data(), 1, d, kLayerNormEps);
+        linear(e, h.data(), 1, d, F, pre + "ffn1", f.data());
+        gelu(f.data(), f.data(), F);
+        linear(e, f.data(), 1, F, d, pre + "ffn2", o.data());
+        for (int64_t i = 0; i < d; ++i) x[i] = x[i] + o[i];
+    }
+    rc.len = t + 1;
+    layer_norm(x.data(), e->p("norm.gamma").data(), e->p("norm.beta").data(), h.data(), 1, d,
+               kLayerNormEps);
+    linear(e, h.data(), 1, d, s.vocabulary, "head", logits);
+}
+
+// Encodes a window from scratch: its real tokens (after the leading PADs) one by one; a window
+// of PADs only is one PAD token at position 0.
+void encode_window(orc_engine* e, RowCache& rc, const std::vector<int32_t>& window, float* logits) {
+    const int64_t W = e->spec.window;
+    const int32_t pad = e->spec.vocabulary;
+    int64_t npad = 0;
+    while (npad < W && window[npad] == pad) ++npad;
+    rc.len = 0;
+    if (npad == W) {
+        cached_step(e, rc, static_cast<float>(pad), 0.0f, logits);
+        return;
+    }
+    for (int64_t t = npad; t < W; ++t) {
+        cached_step(e, rc, static_cast<float>(window[t]), static_cast<float>(t - npad), logits);
+    }
+}
+}  // namespace
+
+extern "C" int32_t orc_generate_batch_cached(orc_engine* e, const int32_t* contexts, int32_t rows,
+                                             int32_t length, int32_t steps, int32_t* produced) {
+    if (e->spec.family != ORC_FAMILY_PADDED_DECODER) {
+        return e->fail(-8, "the cached decode restates the padded decoder only");
+    }
+    int status = require_steps(e, steps);
+    if (status) return status;
+    if (rows < 1) return e->fail(-1, "contexts must not be empty");
+    status = require_context(e, length);
+    if (status) return status;
+    const int64_t W = e->spec.window, d = e->spec.dimension, L = e->spec.layers;
+    const int32_t V = e->spec.vocabulary;
+    for (int32_t r = 0; r < rows; ++r) {
+        const std::vector<int32_t> w = tail(e, contexts + int64_t(r) * length, length);
+        for (int32_t id : w) {
+            if (id < 0 || id > V) return e->fail(-1, "token id outside the vocabulary");
+        }
+    }
+#pragma omp parallel for schedule(dynamic) num_threads(thread_count())
+    for (int32_t r = 0; r < rows; ++r) {
+        std::vector<int32_t> window = tail(e, contexts + int64_t(r) * length, length);
+        RowCache rc;
+        rc.k.assign(static_cast<size_t>(L * W * d), 0.0f);
+        rc.v.assign(static_cast<size_t>(L * W * d), 0.0f);
+        std::vector<float> logits(V);
+        std::vector<double> scores(V);
+        encode_window(e, rc, window, logits.data());
+        for (int32_t step = 0; step < steps; ++step) {
+            for (int32_t v = 0; v < V; ++v) scores[v] = logits[v];
+            const int32_t next = argmax(scores.data(), V);
+            produced[int64_t(r) * steps + step] = next;
+            const bool had_pad = window[0] == V;
+            push(window, next);
+            if (step + 1 == steps) break;
+            if (had_pad && rc.len < W) {
+                cached_step(e, rc, static_cast<float>(next), static_cast<float>(rc.len), logits.data());
+            } else {
+                encode_window(e, rc, window, logits.data());
+            }
+        }
+    }
+    return 0;
+}
+
 // TextEngine.sample / streamSampled (TextEngine.java:201-227, 267-285).
 extern "C" int32_t orc_sample(orc_engine* e, const int32_t* context, int32_t length, int32_t steps,
                               float temperature, int32_t top_k, int32_t* produced, orc_sink sink,

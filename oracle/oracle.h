@@ -101,6 +101,9 @@ int32_t orc_scores_batch(orc_engine* e, const int32_t* contexts, int32_t rows, i
                          double* scores);
 int32_t orc_generate(orc_engine* e, const int32_t* context, int32_t length, int32_t steps,
                      int32_t* produced, orc_sink sink, void* user);
+// Greedy batch decode of the padded decoder with a per-row KV cache (CPU timing baseline).
+int32_t orc_generate_batch_cached(orc_engine* e, const int32_t* contexts, int32_t rows,
+                                  int32_t length, int32_t steps, int32_t* produced);
 int32_t orc_generate_batch(orc_engine* e, const int32_t* contexts, int32_t rows, int32_t length,
                            int32_t steps, int32_t* produced);
 int32_t orc_sample(orc_engine* e, const int32_t* context, int32_t length, int32_t steps,

@@ -97,6 +97,8 @@ def lib() -> ctypes.CDLL:
                                               ctypes.c_int32, i32p, SINK, ctypes.c_void_p]),
             "orc_generate_batch": (ctypes.c_int32, [ctypes.c_void_p, i32p, ctypes.c_int32,
                                                     ctypes.c_int32, ctypes.c_int32, i32p]),
+            "orc_generate_batch_cached": (ctypes.c_int32, [ctypes.c_void_p, i32p, ctypes.c_int32,
+                                                    ctypes.c_int32, ctypes.c_int32, i32p]),
             "orc_sample": (ctypes.c_int32, [ctypes.c_void_p, i32p, ctypes.c_int32,
                                             ctypes.c_int32, ctypes.c_float, ctypes.c_int32, i32p,
                                             SINK, ctypes.c_void_p]),
@@ -319,6 +321,15 @@ class OracleEngine:
         out = np.zeros((arr.shape[0], max(steps, 1)), dtype=np.int32)
         self._check(lib().orc_generate_batch(self._h, _ptr(arr, ctypes.c_int32), arr.shape[0],
                                              arr.shape[1], steps, _ptr(out, ctypes.c_int32)))
+        return out[:, :steps]
+
+    def generate_batch_cached(self, contexts, steps: int) -> np.ndarray:
+        """Greedy batch decode with a per-row KV cache (padded decoder; CPU timing baseline)."""
+        arr = self._contexts(contexts)
+        out = np.zeros((arr.shape[0], max(steps, 1)), dtype=np.int32)
+        self._check(lib().orc_generate_batch_cached(self._h, _ptr(arr, ctypes.c_int32),
+                                                    arr.shape[0], arr.shape[1], steps,
+                                                    _ptr(out, ctypes.c_int32)))
         return out[:, :steps]
 
     def sample(self, context, steps: int, temperature: float, top_k: int,

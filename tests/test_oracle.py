@@ -298,3 +298,24 @@ def test_decoder_window_is_recomputed_every_step():
     e = _tiny_decoder(orc.FAMILY_DECODER)
     np.testing.assert_allclose(e.scores([9, 9, 1, 2, 3, 4, 5, 6, 7, 8]),
                                e.scores([0, 0, 1, 2, 3, 4, 5, 6, 7, 8]), atol=0)
+
+
+def test_cached_decode_agrees_with_full_window_recompute():
+    # The KV-cached CPU decode (a timing baseline) generates what the full-window recompute
+    # generates: the window slides past its PAD prefix (cache extended) and then saturates (the
+    # cached rows re-encode the window), across several rows in parallel.
+    e = _tiny_decoder()
+    V, W = 11, 8
+    rng = np.random.default_rng(3)
+    contexts = np.full((5, W), V, dtype=np.int32)
+    for r, n in enumerate([1, 3, 5, 7, 8]):
+        contexts[r, W - n:] = rng.integers(0, V, size=n)
+    full = e.generate_batch(contexts, 12)
+    cached = e.generate_batch_cached(contexts, 12)
+    np.testing.assert_array_equal(cached, full)
+
+
+def test_cached_decode_serves_the_padded_decoder_only():
+    e = _tiny_decoder(orc.FAMILY_DECODER)
+    with pytest.raises(Exception, match="padded decoder"):
+        e.generate_batch_cached(np.zeros((1, 10), dtype=np.int32), 2)
