@@ -39,6 +39,7 @@ using bst::Epi;
 using bst::EpiArgs;
 
 constexpr float kLayerNormEps = 1e-5f;   // TransformerBlock.java:26,29
+constexpr int kLanes = 4;                // most row groups a batched decode step runs at once
 constexpr int kMaxPrefillTokens = 1 << 17;  // tokens encoded per prefill launch group
 
 thread_local std::string t_last_error;
@@ -316,8 +317,11 @@ struct Workspace {
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
     void *ys_hi = nullptr, *ys_lo = nullptr;  // planes a producer writes for the next projection
     // The second decode lane's operand planes ([rows][max(d, F)]) and split-K partials.
-    void *lane_xs_hi = nullptr, *lane_xs_lo = nullptr, *lane_ys_hi = nullptr, *lane_ys_lo = nullptr;
-    float* lane_part = nullptr;
+    // Lanes 1.. of the batched decode step: operand planes ([rows][max(d, F)]) and split-K
+    // partials of their own.
+    void *lane_xs_hi[kLanes] = {}, *lane_xs_lo[kLanes] = {}, *lane_ys_hi[kLanes] = {},
+         *lane_ys_lo[kLanes] = {};
+    float* lane_part[kLanes] = {};
     int* err = nullptr;                       // tensor-core pipeline error code
     float* tc_part = nullptr;                 // split-K partial products
     unsigned* bar = nullptr;                  // fused decode step: barrier count, head ticket
@@ -347,10 +351,11 @@ class Engine {
     bst_model_spec spec{};
     int device = 0;
     cudaStream_t stream = nullptr;
-    // Second lane of the batched decode step: half of the rows run their layers on stream2 (forked
-    // from and joined back into `stream`), so one half's attention overlaps the other's GEMMs.
-    cudaStream_t stream2 = nullptr;
-    cudaEvent_t lane_fork = nullptr, lane_join = nullptr;
+    // Lanes of the batched decode step: the rows split into up to kLanes groups, lane i > 0 running
+    // its layers on lane_stream[i] (forked from and joined back into `stream`), so the groups'
+    // kernels fill each other's idle SM time.
+    cudaStream_t lane_stream[kLanes] = {};
+    cudaEvent_t lane_fork = nullptr, lane_join[kLanes] = {};
     int V = 0, W = 0, d = 0, L = 0, H = 0, hd = 0, F = 0;
     bool wbf16 = false, kvbf16 = false;
     std::vector<std::string> names;
@@ -420,11 +425,14 @@ class Engine {
         event_pool.clear();
         if (stream) cudaStreamDestroy(stream);
         stream = nullptr;
-        if (stream2) cudaStreamDestroy(stream2);
-        stream2 = nullptr;
+        for (int i = 0; i < kLanes; ++i) {
+            if (lane_stream[i]) cudaStreamDestroy(lane_stream[i]);
+            if (lane_join[i]) cudaEventDestroy(lane_join[i]);
+            lane_stream[i] = nullptr;
+            lane_join[i] = nullptr;
+        }
         if (lane_fork) cudaEventDestroy(lane_fork);
-        if (lane_join) cudaEventDestroy(lane_join);
-        lane_fork = lane_join = nullptr;
+        lane_fork = nullptr;
     }
 
     // ---- launches with optional per-class timing ----
@@ -772,12 +780,14 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
         add(&ws.ys_hi, plane);
         add(&ws.ys_lo, plane);
         if (decoder_family(spec.family)) {
-            const size_t lane_plane = bst::tc_split_bytes(rows, std::max(d, F), wbf16);
-            add(&ws.lane_xs_hi, lane_plane);
-            add(&ws.lane_xs_lo, lane_plane);
-            add(&ws.lane_ys_hi, lane_plane);
-            add(&ws.lane_ys_lo, lane_plane);
-            add(reinterpret_cast<void**>(&ws.lane_part), bst::tc_part_bytes_max());
+            const size_t lane_plane = bst::tc_split_bytes((rows + 1) / 2, std::max(d, F), wbf16);
+            for (int i = 1; i < kLanes; ++i) {
+                add(&ws.lane_xs_hi[i], lane_plane);
+                add(&ws.lane_xs_lo[i], lane_plane);
+                add(&ws.lane_ys_hi[i], lane_plane);
+                add(&ws.lane_ys_lo[i], lane_plane);
+                add(reinterpret_cast<void**>(&ws.lane_part[i]), bst::tc_part_bytes_max());
+            }
         }
         add(reinterpret_cast<void**>(&ws.tc_part), bst::tc_part_bytes_max());
     }
@@ -1127,41 +1137,53 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
                                                        ws.next, ws.len, ws.slot, ws.x, R, d);
                    }), "embedding");
     if (st) return st;
-    const int RA = R / 2;
-    const bool lanes = stream2 && ws.lane_part && RA > 8 && R - RA <= ws.rows &&
-                       linear_on_tc(layers[0].wqkv, RA, 3 * d, d) &&
-                       linear_on_tc(layers[0].wqkv, R - RA, 3 * d, d);
-    if (!lanes) return decode_layers(R, rowmap, lens);
-    // Two lanes: rows [0, RA) on `stream`, rows [RA, R) on stream2 with every per-row workspace
-    // view shifted by RA rows and private planes and partials. Both start together; their
-    // kernels fill each other's idle SM time (starting the second lane a layer phase later, so
-    // that attention meets the other lane's projections, measured slower).
+    // Lanes: BST_DECODE_LANES (1, 2 or 4) in the environment, 2 by default; each lane needs more
+    // than 8 rows (the tensor-core path).
+    int nl = 2;
+    if (const char* env = std::getenv("BST_DECODE_LANES")) nl = std::atoi(env);
+    nl = nl >= 4 ? 4 : nl >= 2 ? 2 : 1;
+    while (nl > 1 && (R / nl <= 8 || !ws.lane_part[nl - 1] ||
+                      !linear_on_tc(layers[0].wqkv, R / nl, 3 * d, d))) {
+        nl /= 2;
+    }
+    if (nl == 1) return decode_layers(R, rowmap, lens);
+    // Lane i takes rows [i R / nl, (i + 1) R / nl) with every per-row workspace view shifted to
+    // them; lanes > 0 run on their own streams with private planes and partials. All start
+    // together (starting lanes a layer phase apart, so that attention meets another lane's
+    // projections, measured slower).
     cudaError_t err = cudaEventRecord(lane_fork, stream);
-    if (!err) err = cudaStreamWaitEvent(stream2, lane_fork, 0);
+    for (int i = 1; i < nl && !err; ++i) err = cudaStreamWaitEvent(lane_stream[i], lane_fork, 0);
     if (err) return cuda_fail(err, "forking the decode lanes");
-    st = decode_layers(RA, rowmap, std::vector<int>(lens.begin(), lens.begin() + RA));
-    if (st) return st;
     const Workspace saved = ws;
     cudaStream_t main = stream;
-    stream = stream2;
-    ws.x += static_cast<size_t>(RA) * d;
-    ws.q += static_cast<size_t>(RA) * d;
-    ws.att += static_cast<size_t>(RA) * d;
-    ws.ffn += static_cast<size_t>(RA) * F;
-    ws.slot += RA;
-    ws.attn_tickets += static_cast<size_t>(RA) * H;
-    ws.part += static_cast<size_t>(RA) * H * ws.splits * (hd + 2);
-    ws.xs_hi = ws.lane_xs_hi;
-    ws.xs_lo = ws.lane_xs_lo;
-    ws.ys_hi = ws.lane_ys_hi;
-    ws.ys_lo = ws.lane_ys_lo;
-    ws.tc_part = ws.lane_part;
-    st = decode_layers(R - RA, rowmap + RA, std::vector<int>(lens.begin() + RA, lens.end()));
+    for (int i = 0; i < nl && !st; ++i) {
+        const int r0 = i * R / nl, r1 = (i + 1) * R / nl;
+        ws = saved;
+        if (i > 0) {
+            stream = lane_stream[i];
+            ws.x += static_cast<size_t>(r0) * d;
+            ws.q += static_cast<size_t>(r0) * d;
+            ws.att += static_cast<size_t>(r0) * d;
+            ws.ffn += static_cast<size_t>(r0) * F;
+            ws.slot += r0;
+            ws.attn_tickets += static_cast<size_t>(r0) * H;
+            ws.part += static_cast<size_t>(r0) * H * ws.splits * (hd + 2);
+            ws.xs_hi = ws.lane_xs_hi[i];
+            ws.xs_lo = ws.lane_xs_lo[i];
+            ws.ys_hi = ws.lane_ys_hi[i];
+            ws.ys_lo = ws.lane_ys_lo[i];
+            ws.tc_part = ws.lane_part[i];
+        }
+        st = decode_layers(r1 - r0, rowmap + r0,
+                           std::vector<int>(lens.begin() + r0, lens.begin() + r1));
+        stream = main;
+    }
     ws = saved;
-    stream = main;
     if (st) return st;
-    err = cudaEventRecord(lane_join, stream2);
-    if (!err) err = cudaStreamWaitEvent(stream, lane_join, 0);
+    for (int i = 1; i < nl && !err; ++i) {
+        err = cudaEventRecord(lane_join[i], lane_stream[i]);
+        if (!err) err = cudaStreamWaitEvent(stream, lane_join[i], 0);
+    }
     return err ? cuda_fail(err, "joining the decode lanes") : BST_OK;
 }
 
@@ -1749,9 +1771,11 @@ int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine
         }
         err = cudaSetDevice(device);
         if (!err) err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
-        if (!err) err = cudaStreamCreateWithFlags(&e->stream2, cudaStreamNonBlocking);
+        for (int i = 1; i < kLanes && !err; ++i) {
+            err = cudaStreamCreateWithFlags(&e->lane_stream[i], cudaStreamNonBlocking);
+            if (!err) err = cudaEventCreateWithFlags(&e->lane_join[i], cudaEventDisableTiming);
+        }
         if (!err) err = cudaEventCreateWithFlags(&e->lane_fork, cudaEventDisableTiming);
-        if (!err) err = cudaEventCreateWithFlags(&e->lane_join, cudaEventDisableTiming);
         if (!err) err = bst::configure_device_kernels_once(device);
         if (err) {
             cudaGetLastError();
