@@ -32,7 +32,6 @@ constexpr int BM = 128;
 constexpr int kRowBytes = 128;                 // one swizzle atom row
 constexpr int kTileRowsA = BM;
 constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s bound on any single wait
-constexpr int kThreads = 192;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -66,17 +65,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase of `bar` with the given parity; false (and an error code) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Waits for the phase of `bar` with the given parity. False on timeout (the error code is
+// recorded and `abort` raised for the other roles of the CTA) or once another role has raised
+// `abort`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_ns();
     while (!mbar_try_wait(bar, parity)) {
+        if (*abort) return false;
         if (global_ns() - start > kWaitNs) {
             atomicCAS(err, 0, code);
+            *abort = 1;
             return false;
         }
     }
     return true;
+}
+
+// Bounded wait that ignores `abort`: used on the way out, to let copies and MMAs already issued
+// finish before their shared memory or TMEM is released.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* err, int code) {
+    const uint64_t start = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - start > kWaitNs) {
+            atomicCAS(err, 0, code);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
@@ -130,18 +150,23 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// 32 consecutive accumulator columns of this thread's TMEM lane (one row of the tile).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 template <int FMT, int BN>
@@ -156,11 +181,161 @@ struct Config {
     static constexpr int kStages = BN == 64 ? 2 : (192 * 1024) / kStageBytes;
     static constexpr int kElemsPerRow = FMT == 2 ? 32 : 64;  // K per stage
     static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
-    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+    // Two accumulators: the epilogue drains one while the MMAs fill the other.
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kCtasPerSm = BN == 64 ? 2 : 1;
 };
 
+constexpr int kEpiWarps = 8;                        // warps 2..9: two per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+__device__ __forceinline__ void st4(float* p, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Writes 32 consecutive values v[0..32) of one row as fp32 (f32 = true) or bf16 to p, which is
+// 16-byte aligned.
+__device__ __forceinline__ void store32(void* p, const float* v, bool f32) {
+    if (f32) {
+        float* q = static_cast<float*>(p);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) st4(q + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+        uint4* q = static_cast<uint4*>(p);
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            q[j / 8] = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
+                                  pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
+        }
+    }
+}
+
+// Operand planes of 32 values (store_split, vectorised): planes = 1 tf32 hi + fp32 remainder,
+// planes = 2 bf16 hi + bf16 remainder.
+__device__ __forceinline__ void store_split32(const float* v, const PlaneOut& po, size_t idx) {
+#pragma unroll
+    for (int g = 0; g < 32; g += 8) {
+        float h[8], l[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (po.planes == 1) {
+                h[j] = __uint_as_float(__float_as_uint(v[g + j]) & 0xFFFFE000u);
+            } else {
+                h[j] = __bfloat162float(__float2bfloat16_rn(v[g + j]));
+            }
+            l[j] = __fsub_rn(v[g + j], h[j]);
+        }
+        if (po.planes == 1) {
+            float* hi = static_cast<float*>(po.hi) + idx + g;
+            float* lo = static_cast<float*>(po.lo) + idx + g;
+            st4(hi, h[0], h[1], h[2], h[3]);
+            st4(hi + 4, h[4], h[5], h[6], h[7]);
+            st4(lo, l[0], l[1], l[2], l[3]);
+            st4(lo + 4, l[4], l[5], l[6], l[7]);
+        } else {
+            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(po.hi) + idx + g) =
+                make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]),
+                           pack_bf16(h[6], h[7]));
+            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(po.lo) + idx + g) =
+                make_uint4(pack_bf16(l[0], l[1]), pack_bf16(l[2], l[3]), pack_bf16(l[4], l[5]),
+                           pack_bf16(l[6], l[7]));
+        }
+    }
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+// True when the 32-column vector epilogue applies to every full chunk of this launch: the
+// destinations are 16-byte aligned with row strides that keep them so, and (kQkv) no chunk
+// straddles a head.
+template <Epi E>
+__device__ __forceinline__ bool vector_epilogue_ok(const EpiArgs& ea, const float* bias, int N,
+                                                   int splits, const float* part) {
+    bool ok = bias == nullptr || aligned16(bias);
+    if (splits > 1) return aligned16(part) && (N % 4) == 0;
+    const bool planes_ok = ea.split.planes == 0 ||
+                           (aligned16(ea.split.hi) && aligned16(ea.split.lo) &&
+                            (ea.split.ld % (ea.split.planes == 1 ? 4 : 8)) == 0);
+    if constexpr (E == Epi::kStore || E == Epi::kGelu) {
+        ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0 && planes_ok;
+    } else if constexpr (E == Epi::kResidual || E == Epi::kLogits) {
+        ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0;
+    } else if constexpr (E == Epi::kResidualGelu) {
+        ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0 && aligned16(ea.res) && (ea.ldr % 4) == 0;
+    } else if constexpr (E == Epi::kQkv) {
+        ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0 && (ea.d % 32) == 0 &&
+             (ea.head_dim % 32) == 0 && aligned16(ea.k_cache) && aligned16(ea.v_cache);
+    }
+    return ok;
+}
+
+// Epilogue of one row's 32 consecutive columns [n, n + 32), all inside the matrix, vector path.
+template <Epi E>
+__device__ __forceinline__ void epilogue32(const EpiArgs& ea, int m, int n, float* v, int M, int N,
+                                           int z, float* part, int row_map, int row_slot) {
+    if (part) {
+        store32(part + static_cast<size_t>(z) * M * N + static_cast<size_t>(m) * N + n, v, true);
+        return;
+    }
+    if constexpr (E == Epi::kStore || E == Epi::kGelu) {
+        if constexpr (E == Epi::kGelu) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_ref(v[j]);
+        }
+        store32(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+        if (ea.split.planes) store_split32(v, ea.split, static_cast<size_t>(m) * ea.split.ld + n);
+    } else if constexpr (E == Epi::kResidual || E == Epi::kResidualGelu) {
+        const float* src = E == Epi::kResidual ? ea.out + static_cast<size_t>(m) * ea.ldo + n
+                                               : ea.res + static_cast<size_t>(m) * ea.ldr + n;
+        float r[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 t = *reinterpret_cast<const float4*>(src + j);
+            r[j] = t.x;
+            r[j + 1] = t.y;
+            r[j + 2] = t.z;
+            r[j + 3] = t.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            v[j] = E == Epi::kResidual ? __fadd_rn(r[j], v[j]) : gelu_ref(__fadd_rn(v[j], r[j]));
+        }
+        store32(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+    } else if constexpr (E == Epi::kQkv) {
+        if (n < ea.d) {
+            store32(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+        } else {
+            const int which = n / ea.d;
+            const int j = n - which * ea.d;
+            const int h = j / ea.head_dim;
+            const int e = j - h * ea.head_dim;
+            const size_t idx =
+                ((static_cast<size_t>(row_map) * ea.heads + h) * ea.slots + row_slot) * ea.head_dim + e;
+            void* base = which == 1 ? ea.k_cache : ea.v_cache;
+            if (ea.kv_bf16) {
+                store32(static_cast<__nv_bfloat16*>(base) + idx, v, false);
+            } else {
+                store32(static_cast<float*>(base) + idx, v, true);
+            }
+        }
+    } else if constexpr (E == Epi::kLogits) {
+        store32(ea.out + static_cast<size_t>(row_map) * ea.ldo + n, v, true);
+    }
+}
+
+// Persistent tcgen05 GEMM. Work units are (n tile, m tile, k split), n fastest so that the CTAs
+// running at one time share A rows in L2; CTA b takes units b, b + gridDim.x, ... Warp 0 streams
+// k-tiles of all its units through the shared-memory ring, warp 1 issues the MMAs of unit i into
+// accumulator i % 2, and the eight epilogue warps drain the other accumulator meanwhile.
 template <int FMT, int BN, Epi E>
-__global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
+__global__ __launch_bounds__(kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_tc(
     const __grid_constant__ CUtensorMap a0, const __grid_constant__ CUtensorMap a1,
     const __grid_constant__ CUtensorMap b0, const __grid_constant__ CUtensorMap b1,
     const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err, int splits,
@@ -171,23 +346,31 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + C::kStages * C::kStageBytes);
     uint64_t* empty = full + C::kStages;
-    uint64_t* acc_full = empty + C::kStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* acc_full = empty + C::kStages;     // [2]
+    uint64_t* acc_empty = acc_full + 2;          // [2]
+    uint64_t* drained = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    // Split-K: this CTA accumulates k-tiles [kt0, kt1) (the host makes every split non-empty).
+    const int tiles_n = (N + BN - 1) / BN, tiles_m = (M + BM - 1) / BM;
+    const int units = tiles_n * tiles_m * splits;
+    // Split-K: split z accumulates k-tiles [z * per, min(k_total, (z + 1) * per)); the host makes
+    // every split non-empty.
     const int k_total = (K + C::kElemsPerRow - 1) / C::kElemsPerRow;
     const int per = (k_total + splits - 1) / splits;
-    const int kt0 = blockIdx.z * per;
-    const int k_tiles = min(k_total, kt0 + per) - kt0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kEpiWarps);
+        }
+        mbar_init(drained, 1);
+        *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -207,96 +390,139 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_tc(
     auto stage_b = [&](int s, int p) {
         return base + s * C::kStageBytes + C::kPlanesA * C::kBytesA + p * C::kBytesB;
     };
+    auto unit_coords = [&](int u, int* m0, int* n0, int* z) {
+        *n0 = (u % tiles_n) * BN;
+        const int rest = u / tiles_n;
+        *m0 = (rest % tiles_m) * BM;
+        *z = rest / tiles_m;
+    };
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
+            int it = 0;
             bool ok = true;
-            for (int kt = 0; kt < k_tiles && ok; ++kt) {
-                const int s = kt % C::kStages;
-                const uint32_t phase = (kt / C::kStages) & 1;
-                ok = mbar_wait(&empty[s], phase ^ 1, err, 1);
-                if (!ok) break;
-                mbar_expect_tx(&full[s], C::kStageBytes);
-                const int kx = (kt0 + kt) * C::kElemsPerRow;
-                tma_load_2d(&a0, &full[s], stage_a(s, 0), kx, m0);
-                tma_load_2d(&a1, &full[s], stage_a(s, 1), kx, m0);
-                tma_load_2d(&b0, &full[s], stage_b(s, 0), kx, n0);
-                if constexpr (C::kPlanesB == 2) tma_load_2d(&b1, &full[s], stage_b(s, 1), kx, n0);
-                ++issued;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                int m0, n0, z;
+                unit_coords(u, &m0, &n0, &z);
+                const int kt0 = z * per, kt1 = min(k_total, kt0 + per);
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t phase = (it / C::kStages) & 1;
+                    ok = mbar_wait(&empty[s], phase ^ 1, err, 1, abort);
+                    if (!ok) break;
+                    mbar_expect_tx(&full[s], C::kStageBytes);
+                    const int kx = kt * C::kElemsPerRow;
+                    tma_load_2d(&a0, &full[s], stage_a(s, 0), kx, m0);
+                    tma_load_2d(&a1, &full[s], stage_a(s, 1), kx, m0);
+                    tma_load_2d(&b0, &full[s], stage_b(s, 0), kx, n0);
+                    if constexpr (C::kPlanesB == 2) tma_load_2d(&b1, &full[s], stage_b(s, 1), kx, n0);
+                }
             }
             if (!ok) {
                 // Drain this CTA's copies still in flight before shared memory goes away.
-                for (int kt = (issued > C::kStages ? issued - C::kStages : 0); kt < issued; ++kt) {
-                    mbar_wait(&full[kt % C::kStages], (kt / C::kStages) & 1, err, 1);
+                for (int i = (it > C::kStages ? it - C::kStages : 0); i < it; ++i) {
+                    mbar_drain(&full[i % C::kStages], (i / C::kStages) & 1, err, 1);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = instr_desc<FMT, BN>();
+            int it = 0, local = 0;
             bool ok = true;
-            for (int kt = 0; kt < k_tiles; ++kt) {
-                const int s = kt % C::kStages;
-                const uint32_t phase = (kt / C::kStages) & 1;
-                ok = mbar_wait(&full[s], phase, err, 2);
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+                int m0, n0, z;
+                unit_coords(u, &m0, &n0, &z);
+                const int kt0 = z * per, kt1 = min(k_total, kt0 + per);
+                const int buf = local & 1;
+                ok = mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, err, 4, abort);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + static_cast<uint32_t>(buf * BN);
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t phase = (it / C::kStages) & 1;
+                    ok = mbar_wait(&full[s], phase, err, 2, abort);
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
+                    for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-                    for (int pass = 0; pass < C::kPasses; ++pass) {
-                        // tf32: (Xh,Wh), (Xh,Wl), (Xl,Wh); bf16: (Xh,W), (Xl,W).
-                        const int pa = (FMT == 2) ? (pass == 2 ? 1 : 0) : pass;
-                        const int pb = (FMT == 2) ? (pass == 1 ? 1 : 0) : 0;
-                        const uint64_t ad = smem_desc(smem_u32(stage_a(s, pa)) + kk * 32);
-                        const uint64_t bd = smem_desc(smem_u32(stage_b(s, pb)) + kk * 32);
-                        mma<FMT>(tmem, ad, bd, idesc, (kt | kk | pass) != 0);
+                        for (int pass = 0; pass < C::kPasses; ++pass) {
+                            // tf32: (Xh,Wh), (Xh,Wl), (Xl,Wh); bf16: (Xh,W), (Xl,W).
+                            const int pa = (FMT == 2) ? (pass == 2 ? 1 : 0) : pass;
+                            const int pb = (FMT == 2) ? (pass == 1 ? 1 : 0) : 0;
+                            const uint64_t ad = smem_desc(smem_u32(stage_a(s, pa)) + kk * 32);
+                            const uint64_t bd = smem_desc(smem_u32(stage_b(s, pb)) + kk * 32);
+                            mma<FMT>(acc, ad, bd, idesc, (kt != kt0) | kk | pass);
+                        }
                     }
+                    mma_commit(&empty[s]);
                 }
-                mma_commit(&empty[s]);
+                if (!ok) break;
+                mma_commit(&acc_full[buf]);
             }
-            if (ok) mma_commit(acc_full);
-            else atomicCAS(err, 0, 2);
+            // Every MMA issued above completes before the accumulators are released.
+            mma_commit(drained);
+            mbar_drain(drained, 0, err, 5);
         }
     } else {
-        // Epilogue warps 2..5 own TMEM lane quarters (warp % 4).
+        // Epilogue warps: TMEM lane quarter warp % 4 (rows), column half (warp - 2) / 4.
         const int quarter = warp & 3;
-        const bool ok = mbar_wait(acc_full, 0, err, 3);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // Stage the 128 x BN tile through shared memory (the drained pipeline ring), so the
-        // global traffic below is row-coalesced.
-        float* tile = reinterpret_cast<float*>(base);
-        constexpr int LD = BN + 1;
-        if (__all_sync(0xffffffffu, ok)) {
-            const int r = quarter * 32 + lane;
-            const uint32_t row_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 16) {
-                float v[16];
-                tmem_ld16(row_addr + c, v);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) tile[r * LD + c + j] = v[j];
-            }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const int t = threadIdx.x - 64;
-        if (splits > 1) {
-            float* out = part + static_cast<size_t>(blockIdx.z) * M * N;
-            for (int e = t; e < BM * BN; e += 128) {
-                const int r = e / BN, c = e - r * BN;
-                const int m = m0 + r, n = n0 + c;
-                if (m < M && n < N) out[static_cast<size_t>(m) * N + n] = tile[r * LD + c];
-            }
-        } else {
-            for (int e = t; e < BM * BN; e += 128) {
-                const int r = e / BN, c = e - r * BN;
-                const int m = m0 + r, n = n0 + c;
-                if (m < M && n < N) {
-                    const float v = tile[r * LD + c];
-                    epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, bias[n]) : v);
+        const int half = (warp - 2) >> 2;
+        const bool vec = vector_epilogue_ok<E>(ea, bias, N, splits, part);
+        int local = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+            int m0, n0, z;
+            unit_coords(u, &m0, &n0, &z);
+            const int buf = local & 1;
+            const bool ok = mbar_wait(&acc_full[buf], (local >> 1) & 1, err, 3, abort);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int m = m0 + quarter * 32 + lane;
+            int row_map = 0, row_slot = 0;
+            if constexpr (E == Epi::kQkv || E == Epi::kLogits) {
+                if (splits == 1 && m < M) {
+                    row_map = ea.rowmap[m];
+                    if constexpr (E == Epi::kQkv) row_slot = ea.slot[m];
                 }
             }
+            const uint32_t row_addr =
+                tmem + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+                float v[32];
+                tmem_ld32(row_addr + c, v);
+                const int n = n0 + c;
+                if (m < M && n < N) {
+                if (splits == 1 && bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (n + j < N) v[j] = __fadd_rn(v[j], __ldg(bias + n + j));
+                    }
+                }
+                if (vec && n + 32 <= N) {
+                    epilogue32<E>(ea, m, n, v, M, N, z, splits > 1 ? part : nullptr, row_map,
+                                  row_slot);
+                } else if (splits > 1) {
+                    float* out = part + static_cast<size_t>(z) * M * N + static_cast<size_t>(m) * N;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (n + j < N) out[n + j] = v[j];
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (n + j < N) epi_apply<E>(ea, m, n + j, v[j]);
+                    }
+                }
+                }
+                __syncwarp();
+            }
+            // This warp's reads of the accumulator are done: hand it back to the MMA warp.
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -359,6 +585,17 @@ __global__ void k_split_bf16(const float* __restrict__ x, int ldx, int M, int K,
     }
 }
 
+// Streaming multiprocessors of the current device (the persistent grid's size).
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        return 148;
+    }
+    return n;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
@@ -403,7 +640,8 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
                          const CUtensorMap& b0, const CUtensorMap& b1, const float* bias, int M,
                          int N, int K, const EpiArgs& ea, int* err, const SplitK& sk) {
     using C = Config<FMT, BN>;
-    const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits);
+    const long units = static_cast<long>((N + BN - 1) / BN) * ((M + BM - 1) / BM) * sk.splits;
+    const dim3 grid(static_cast<unsigned>(std::min<long>(units, static_cast<long>(sm_count()) * C::kCtasPerSm)));
     cudaError_t e = launch_pdl(k_gemm_tc<FMT, BN, E>, grid, dim3(kThreads), C::kSmem, s, a0, a1, b0,
                                b1, bias, M, N, K, ea, err, sk.splits, sk.part);
     if (e != cudaSuccess || sk.splits == 1 || sk.defer) return e;

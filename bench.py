@@ -253,6 +253,70 @@ def batch1(local, steps, warmup):
             "peak_source": src}
 
 
+def other_configs(local, reps=3):
+    """The other workloads of the scope table, timed on the device: C1 and C2 as per-call latency
+    (L2-resident models), C3 with bf16 weights as decode tokens/s."""
+    import torch
+
+    from basalt_b200 import (Basalt, TextEngine, config, left_pad, synthetic_prompts,
+                             write_synthetic_weights)
+
+    from dataclasses import replace
+
+    out = {}
+    for name in ("v96-d128-l2-w64-b1-greedy", "v96-d256-l4-w128-b32-greedy",
+                 "v96-d256-l4-w128-b32-sampled", "v4096-d512-l6-w512-b256-greedy-bf16w",
+                 "v8192-d768-l12-w1024-n8192-sampled-bf16w"):
+        w = config(name)
+        if w.rows > 4096:
+            # 8192 sequences in waves of max_rows: 64 of the 512 tokens per row keep the call short
+            w = replace(w, steps=64)
+        m = w.model
+        with tempfile.TemporaryDirectory() as tmp:
+            path = Path(tmp) / "w.bin"
+            write_synthetic_weights(m, path, w.weight_seed)
+            engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
+            engine.load(path)
+        ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
+                       m.vocabulary)
+        stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
+        d_ctx = torch.from_numpy(ctx).to(f"cuda:{local}")
+        d_tok = torch.empty((w.rows, w.steps), dtype=torch.int32, device=f"cuda:{local}")
+        d_one = torch.empty((w.rows, 1), dtype=torch.int32, device=f"cuda:{local}")
+
+        def call(n, dst):
+            if w.mode == "sample":
+                engine.seed(w.sample_seed)
+                engine.sample_device(d_ctx.data_ptr(), w.rows, ctx.shape[1], n, w.temperature,
+                                     w.k, dst.data_ptr())
+            else:
+                engine.generate_device(d_ctx.data_ptr(), w.rows, ctx.shape[1], n, dst.data_ptr())
+
+        n_reps = 1 if w.rows > 4096 else reps
+
+        def timed(n, dst):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(n_reps):
+                call(n, dst)
+            b.record(stream)
+            b.synchronize()
+            return a.elapsed_time(b) / n_reps
+
+        call(w.steps, d_tok)
+        call(1, d_one)
+        torch.cuda.synchronize()
+        full_ms = timed(w.steps, d_tok)
+        first_ms = timed(1, d_one)
+        decode_ms = (full_ms - first_ms) / max(1, w.steps - 1)
+        out[name] = {"rows": w.rows, "new_tokens": w.steps, "ms_per_call": full_ms,
+                     "prefill_ms": first_ms, "decode_ms_per_step": decode_ms,
+                     "tokens_per_s": w.rows * w.steps / (full_ms / 1000.0),
+                     "decode_tokens_per_s": w.rows / (decode_ms / 1000.0) if decode_ms > 0 else None}
+        engine.close()
+    return out
+
+
 def run_reference(args, rank, world):
     from basalt_b200 import config, write_synthetic_weights
 
@@ -473,6 +537,7 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_batch1:
         line["batch1"] = batch1(local, max(1, args.steps), max(1, args.warmup))
+        line["configs"] = other_configs(local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(workload, wpath)
     if dist:

@@ -59,7 +59,10 @@ def test_gemm_unit_cases(runtime, known):
 
 @pytest.mark.parametrize("m,k,n", [(1, 768, 2304), (5, 300, 77), (8, 512, 512), (9, 64, 16),
                                    (33, 36, 9), (100, 512, 1536), (256, 2048, 512),
-                                   (300, 120, 200), (1024, 768, 3072)])
+                                   (300, 120, 200), (1024, 768, 3072),
+                                   # more tiles than SMs: CTAs loop over units and alternate
+                                   # accumulators; tails in M, N and K
+                                   (3000, 200, 1000), (4096, 512, 1536)])
 def test_random_shapes_match_fp32(runtime, m, k, n):
     rng = np.random.default_rng(m * 1000 + n)
     a = rng.standard_normal((m, k)).astype(np.float32)
