@@ -638,91 +638,188 @@ __global__ __launch_bounds__(128) void k_attn_decode(
 
 // ---------------------------------------------------------------------------------------------
 // Causal prefill attention over one row's freshly written cache slots. CTA = (segment, head,
-// tile of 4*QPW queries); keys stream through shared memory 32 at a time with an online softmax.
+// tile of 64 queries), 256 threads; keys stream through shared memory 64 at a time with an online
+// softmax. Register tiling: thread (ty, tx) = (tid / 16, tid % 16) owns queries 4ty..4ty+3 of the
+// tile, their scores against keys 4tx..4tx+3 of the chunk, and output columns 64c + 4tx..+3
+// (HD >= 64) or 2tx, 2tx+1 (HD = 32). Shared memory holds Q and K transposed ([e][query|key]) so
+// both score operands are float4 reads, V as [key][e], and the probabilities transposed
+// ([key][query]) with the query group XOR-swizzled by key / 4, which makes the 16 float4 stores
+// of a half warp hit distinct bank groups.
 // ---------------------------------------------------------------------------------------------
-template <typename KT, int HD, int QPW>
-__global__ __launch_bounds__(128) void k_attn_prefill(
+constexpr int kPrefillTile = 64;
+
+template <int HD>
+constexpr int attn_prefill_smem() {
+    return (3 * HD * kPrefillTile + kPrefillTile * kPrefillTile) * static_cast<int>(sizeof(float));
+}
+
+__device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(bf16_bits_to_f(u.x & 0xffffu), bf16_bits_to_f(u.x >> 16),
+                       bf16_bits_to_f(u.y & 0xffffu), bf16_bits_to_f(u.y >> 16));
+}
+
+template <typename KT, int HD>
+__global__ __launch_bounds__(256, HD > 64 ? 2 : 3) void k_attn_prefill(
     const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
     const int* __restrict__ seg_row, const int* __restrict__ seg_start,
     const int* __restrict__ seg_len, int heads, int slots, float scale, float* __restrict__ out,
     PlaneOut po) {
     pdl_trigger();
     pdl_wait();
-    constexpr int QT = 4 * QPW;
-    constexpr int DPL = HD / 32;
-    const int j = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * QT;
+    constexpr int T = kPrefillTile;
+    constexpr int OC = HD / 16;  // output columns per thread
+    extern __shared__ __align__(16) float smem_f[];
+    float* Qt = smem_f;         // [HD][T]
+    float* Kt = Qt + HD * T;    // [HD][T]
+    float* Vs = Kt + HD * T;    // [T][HD]
+    float* Pt = Vs + T * HD;    // [T][T], swizzled
+    const int j = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * T;
     const int n = seg_len[j];
     if (t0 >= n) return;
     const int row = seg_row[j], start = seg_start[j], d = heads * HD;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ float Qs[QT][HD];
-    __shared__ float Kt[HD][33];
-    __shared__ float Vs[32][HD];
-    for (int idx = tid; idx < QT * HD; idx += 128) {
-        const int r = idx / HD, e = idx - r * HD;
-        const int t = t0 + r;
-        Qs[r][e] = t < n ? q[static_cast<size_t>(start + t) * d + h * HD + e] : 0.0f;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+
+    // Q tile, transposed; lanes run along queries so the transposed stores are conflict-free.
+    for (int idx = tid; idx < T * (HD / 4); idx += 256) {
+        const int r = idx % T, e4 = idx / T;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (t0 + r < n) v = load4(q + static_cast<size_t>(start + t0 + r) * d + h * HD + 4 * e4);
+        Qt[(4 * e4 + 0) * T + r] = v.x;
+        Qt[(4 * e4 + 1) * T + r] = v.y;
+        Qt[(4 * e4 + 2) * T + r] = v.z;
+        Qt[(4 * e4 + 3) * T + r] = v.w;
     }
-    float m[QPW], l[QPW], o[QPW][DPL];
+    float m[4], l[4], o[4][OC];
 #pragma unroll
-    for (int r = 0; r < QPW; ++r) {
-        m[r] = -INFINITY;
-        l[r] = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < DPL; ++c) o[r][c] = 0.0f;
+        for (int c = 0; c < OC; ++c) o[i][c] = 0.0f;
     }
     const size_t base = (static_cast<size_t>(row) * heads + h) * slots;
-    const int kend = min(n, t0 + QT);
-    for (int kb = 0; kb < kend; kb += 32) {
-        __syncthreads();
-        for (int idx = tid; idx < 32 * HD; idx += 128) {
-            const int r = idx / HD, e = idx - r * HD;
-            const int key = kb + r;
-            float kv = 0.0f, vv = 0.0f;
-            if (key < n) {
-                kv = to_f(kc[(base + key) * HD + e]);
-                vv = to_f(vc[(base + key) * HD + e]);
-            }
-            Kt[e][r] = kv;
-            Vs[r][e] = vv;
+    const int kend = min(n, t0 + T);
+    for (int kb = 0; kb < kend; kb += T) {
+        __syncthreads();  // the previous chunk's K, V and P are no longer read
+        for (int idx = tid; idx < T * (HD / 4); idx += 256) {
+            const int r = idx % T, e4 = idx / T;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (kb + r < n) v = load4(kc + (base + kb + r) * HD + 4 * e4);
+            Kt[(4 * e4 + 0) * T + r] = v.x;
+            Kt[(4 * e4 + 1) * T + r] = v.y;
+            Kt[(4 * e4 + 2) * T + r] = v.z;
+            Kt[(4 * e4 + 3) * T + r] = v.w;
+        }
+        for (int idx = tid; idx < T * (HD / 4); idx += 256) {
+            const int e4 = idx % (HD / 4), r = idx / (HD / 4);
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (kb + r < n) v = load4(vc + (base + kb + r) * HD + 4 * e4);
+            *reinterpret_cast<float4*>(Vs + r * HD + 4 * e4) = v;
         }
         __syncthreads();
-        const int key = kb + lane;
+
+        float sc[4][4];
 #pragma unroll
-        for (int r = 0; r < QPW; ++r) {
-            const int qi = warp * QPW + r;
-            const int t = t0 + qi;
-            float s = -INFINITY;
-            if (t < n && key <= t) {
-                float dot = 0.0f;
-#pragma unroll 16
-                for (int e = 0; e < HD; ++e) dot = fmaf(Qs[qi][e], Kt[e][lane], dot);
-                s = __fmul_rn(dot, scale);
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.0f;
+        }
+#pragma unroll 8
+        for (int e = 0; e < HD; ++e) {
+            const float4 qa = *reinterpret_cast<const float4*>(Qt + e * T + 4 * ty);
+            const float4 ka = *reinterpret_cast<const float4*>(Kt + e * T + 4 * tx);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w};
+            const float kv[4] = {ka.x, ka.y, ka.z, ka.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qv[i], kv[jj], sc[i][jj]);
             }
-            const float mnew = fmaxf(m[r], warp_max(s));
-            if (mnew == -INFINITY) continue;
-            const float p = s == -INFINITY ? 0.0f : expf(s - mnew);
-            const float corr = m[r] == -INFINITY ? 0.0f : expf(m[r] - mnew);
-            l[r] = l[r] * corr + warp_sum(p);
+        }
+
+        // Online softmax per query row; a row's 64 scores live in the 16 lanes sharing ty.
+        float p[4][4];
 #pragma unroll
-            for (int c = 0; c < DPL; ++c) o[r][c] *= corr;
-            for (int kk = 0; kk < 32; ++kk) {
-                const float pk = __shfl_sync(kFull, p, kk);
+        for (int i = 0; i < 4; ++i) {
+            const int t = t0 + 4 * ty + i;
+            float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < DPL; ++c) o[r][c] = fmaf(pk, Vs[kk][lane * DPL + c], o[r][c]);
+            for (int jj = 0; jj < 4; ++jj) {
+                const int key = kb + 4 * tx + jj;
+                sc[i][jj] = (t < n && key <= t) ? __fmul_rn(sc[i][jj], scale) : -INFINITY;
+                mx = fmaxf(mx, sc[i][jj]);
             }
-            m[r] = mnew;
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+            const float mnew = fmaxf(m[i], mx);
+            float corr = 1.0f, ps = 0.0f;
+            if (mnew == -INFINITY) {
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) p[i][jj] = 0.0f;
+            } else {
+                corr = m[i] == -INFINITY ? 0.0f : expf(m[i] - mnew);
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    p[i][jj] = sc[i][jj] == -INFINITY ? 0.0f : expf(sc[i][jj] - mnew);
+                    ps += p[i][jj];
+                }
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) ps += __shfl_xor_sync(kFull, ps, off);
+            l[i] = l[i] * corr + ps;
+#pragma unroll
+            for (int c = 0; c < OC; ++c) o[i][c] *= corr;
+            m[i] = mnew;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int k = 4 * tx + jj;
+            *reinterpret_cast<float4*>(Pt + k * T + ((ty ^ (k >> 2)) << 2)) =
+                make_float4(p[0][jj], p[1][jj], p[2][jj], p[3][jj]);
+        }
+        __syncthreads();
+
+        const int kn = min(T, kend - kb);
+#pragma unroll 4
+        for (int k = 0; k < kn; ++k) {
+            const float4 pa = *reinterpret_cast<const float4*>(Pt + k * T + ((ty ^ (k >> 2)) << 2));
+            const float pv[4] = {pa.x, pa.y, pa.z, pa.w};
+            if constexpr (HD == 32) {
+                const float2 vb = *reinterpret_cast<const float2*>(Vs + k * HD + 2 * tx);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    o[i][0] = fmaf(pv[i], vb.x, o[i][0]);
+                    o[i][1] = fmaf(pv[i], vb.y, o[i][1]);
+                }
+            } else {
+#pragma unroll
+                for (int c4 = 0; c4 < HD / 64; ++c4) {
+                    const float4 vb = *reinterpret_cast<const float4*>(Vs + k * HD + 64 * c4 + 4 * tx);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        o[i][4 * c4 + 0] = fmaf(pv[i], vb.x, o[i][4 * c4 + 0]);
+                        o[i][4 * c4 + 1] = fmaf(pv[i], vb.y, o[i][4 * c4 + 1]);
+                        o[i][4 * c4 + 2] = fmaf(pv[i], vb.z, o[i][4 * c4 + 2]);
+                        o[i][4 * c4 + 3] = fmaf(pv[i], vb.w, o[i][4 * c4 + 3]);
+                    }
+                }
+            }
         }
     }
 #pragma unroll
-    for (int r = 0; r < QPW; ++r) {
-        const int t = t0 + warp * QPW + r;
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + 4 * ty + i;
         if (t >= n) continue;
+        float* dst = out + static_cast<size_t>(start + t) * d + h * HD;
+        const size_t at0 = static_cast<size_t>(start + t) * d + h * HD;
 #pragma unroll
-        for (int c = 0; c < DPL; ++c) {
-            const size_t at = static_cast<size_t>(start + t) * d + h * HD + lane * DPL + c;
-            out[at] = o[r][c] / l[r];
-            if (po.planes) store_split(o[r][c] / l[r], po.planes, po.hi, po.lo, at);
+        for (int c = 0; c < OC; ++c) {
+            const int col = HD == 32 ? 2 * tx + c : 64 * (c / 4) + 4 * tx + (c % 4);
+            const float v = o[i][c] / l[i];
+            dst[col] = v;
+            if (po.planes) store_split(v, po.planes, po.hi, po.lo, at0 + col);
         }
     }
 }
@@ -994,9 +1091,8 @@ cudaError_t attn_prefill_typed(cudaStream_t s, const float* q, const void* kc, c
                                const int* seg_row, const int* seg_start, const int* seg_len,
                                int segments, int max_len, int heads, int slots, float scale,
                                float* out, const PlaneOut& po) {
-    constexpr int QPW = HD > 64 ? 4 : 8;
-    const dim3 grid(segments, heads, (max_len + 4 * QPW - 1) / (4 * QPW));
-    return launch_pdl(k_attn_prefill<KT, HD, QPW>, grid, 128, 0, s,
+    const dim3 grid(segments, heads, (max_len + kPrefillTile - 1) / kPrefillTile);
+    return launch_pdl(k_attn_prefill<KT, HD>, grid, 256, attn_prefill_smem<HD>(), s,
         q, static_cast<const KT*>(kc), static_cast<const KT*>(vc), seg_row, seg_start, seg_len,
         heads, slots, scale, out, po);
 }
@@ -1133,11 +1229,25 @@ cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, 
                                              done, tokens, next, window);
 }
 
+namespace {
+template <typename KT, int HD>
+cudaError_t configure_attn_prefill() {
+    return cudaFuncSetAttribute(k_attn_prefill<KT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                attn_prefill_smem<HD>());
+}
+}  // namespace
+
 cudaError_t configure_device_kernels() {
     cudaError_t err = cudaFuncSetAttribute(k_select_sample,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(kSampleSmemLimit));
     if (err != cudaSuccess) return err;
+    if ((err = configure_attn_prefill<float, 32>()) != cudaSuccess) return err;
+    if ((err = configure_attn_prefill<float, 64>()) != cudaSuccess) return err;
+    if ((err = configure_attn_prefill<float, 128>()) != cudaSuccess) return err;
+    if ((err = configure_attn_prefill<__nv_bfloat16, 32>()) != cudaSuccess) return err;
+    if ((err = configure_attn_prefill<__nv_bfloat16, 64>()) != cudaSuccess) return err;
+    if ((err = configure_attn_prefill<__nv_bfloat16, 128>()) != cudaSuccess) return err;
     return configure_tc_kernels();
 }
 
