@@ -9,10 +9,14 @@
 //     X = Xh + Xl likewise (split per call); Y = Xh*Wh + Xh*Wl + Xl*Wh, fp32 accumulation.
 //   * bf16 weights: X = Xh + Xl as two bf16 planes; Y = Xh*W + Xl*W (kind::f16, bf16 inputs).
 //
-// Tile: 128 x BN output per CTA (BN = 64 or 128), K staged in 128-byte rows (32 fp32 / 64 bf16)
-// with the 128-byte swizzle. Warp 0 issues TMA, warp 1 owns TMEM and issues the MMAs, warps 2-5
-// drain TMEM (each warp reads its 32-lane quarter) and apply the epilogue. Every mbarrier wait is
-// bounded in time; on expiry the kernel records an error code, drains its own copies and returns.
+// Tile: 128 x BN outputs (BN = 64 or 128), K staged in 128-byte rows (32 fp32 / 64 bf16) with the
+// 128-byte swizzle. Two kernels share the tile machinery: k_gemm_tc runs one work unit (tile,
+// k split) per CTA when all units fit in one wave (the decode GEMMs); k_gemm_tc_persistent loops
+// each resident CTA over the units of larger GEMMs (prefill), with two TMEM accumulators so that
+// the epilogue of one tile overlaps the MMAs of the next. In both, warp 0 issues TMA, warp 1
+// owns TMEM and issues the MMAs, and the remaining warps drain TMEM (each warp reads its 32-lane
+// quarter). Every mbarrier wait is bounded in time; on expiry the kernel records an error code,
+// stops its other roles, drains its own copies and MMAs, and returns.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -150,23 +154,35 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// 32 consecutive accumulator columns of this thread's TMEM lane (one row of the tile).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr));
+// CW (16 or 32) consecutive accumulator columns of this thread's TMEM lane (one row of the tile).
+template <int CW>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v) {
+    uint32_t r[CW];
+    if constexpr (CW == 32) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+            "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+            "%28, %29, %30, %31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+              "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+              "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+              "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+              "=r"(r[31])
+            : "r"(taddr));
+    } else {
+        static_assert(CW == 16, "chunk width");
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+            "%11, %12, %13, %14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+              "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+    }
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < CW; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 template <int FMT, int BN>
@@ -181,13 +197,19 @@ struct Config {
     static constexpr int kStages = BN == 64 ? 2 : (192 * 1024) / kStageBytes;
     static constexpr int kElemsPerRow = FMT == 2 ? 32 : 64;  // K per stage
     static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
-    // Two accumulators: the epilogue drains one while the MMAs fill the other.
+    // Two accumulators for the persistent variant: the epilogue drains one while the MMAs fill
+    // the other.
     static constexpr int kTmemCols = 2 * BN;
     static constexpr int kCtasPerSm = BN == 64 ? 2 : 1;
+    // Epilogue warps 2.. cover the four TMEM lane quarters kColGroups times over, each warp a
+    // column range of BN / kColGroups drained CW columns at a time. The narrow decode tiles keep
+    // a small footprint (192 threads, 16-column chunks) so that two CTAs and the other decode
+    // lane's kernels share an SM.
+    static constexpr int kColGroups = BN == 64 ? 1 : 2;
+    static constexpr int kEpiWarps = 4 * kColGroups;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
+    static constexpr int CW = BN == 64 ? 16 : 32;
 };
-
-constexpr int kEpiWarps = 8;                        // warps 2..9: two per TMEM lane quarter
-constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 __device__ __forceinline__ void st4(float* p, float a, float b, float c, float d) {
     *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
@@ -198,28 +220,30 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Writes 32 consecutive values v[0..32) of one row as fp32 (f32 = true) or bf16 to p, which is
+// Writes CW consecutive values v[0..CW) of one row as fp32 (f32 = true) or bf16 to p, which is
 // 16-byte aligned.
-__device__ __forceinline__ void store32(void* p, const float* v, bool f32) {
+template <int CW>
+__device__ __forceinline__ void store_row(void* p, const float* v, bool f32) {
     if (f32) {
         float* q = static_cast<float*>(p);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) st4(q + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        for (int j = 0; j < CW; j += 4) st4(q + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
     } else {
         uint4* q = static_cast<uint4*>(p);
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
+        for (int j = 0; j < CW; j += 8) {
             q[j / 8] = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
                                   pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
         }
     }
 }
 
-// Operand planes of 32 values (store_split, vectorised): planes = 1 tf32 hi + fp32 remainder,
+// Operand planes of CW values (store_split, vectorised): planes = 1 tf32 hi + fp32 remainder,
 // planes = 2 bf16 hi + bf16 remainder.
-__device__ __forceinline__ void store_split32(const float* v, const PlaneOut& po, size_t idx) {
+template <int CW>
+__device__ __forceinline__ void store_split_row(const float* v, const PlaneOut& po, size_t idx) {
 #pragma unroll
-    for (int g = 0; g < 32; g += 8) {
+    for (int g = 0; g < CW; g += 8) {
         float h[8], l[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -252,10 +276,10 @@ __device__ __forceinline__ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
-// True when the 32-column vector epilogue applies to every full chunk of this launch: the
+// True when the CW-column vector epilogue applies to every full chunk of this launch: the
 // destinations are 16-byte aligned with row strides that keep them so, and (kQkv) no chunk
 // straddles a head.
-template <Epi E>
+template <Epi E, int CW>
 __device__ __forceinline__ bool vector_epilogue_ok(const EpiArgs& ea, const float* bias, int N,
                                                    int splits, const float* part) {
     bool ok = bias == nullptr || aligned16(bias);
@@ -270,33 +294,33 @@ __device__ __forceinline__ bool vector_epilogue_ok(const EpiArgs& ea, const floa
     } else if constexpr (E == Epi::kResidualGelu) {
         ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0 && aligned16(ea.res) && (ea.ldr % 4) == 0;
     } else if constexpr (E == Epi::kQkv) {
-        ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0 && (ea.d % 32) == 0 &&
-             (ea.head_dim % 32) == 0 && aligned16(ea.k_cache) && aligned16(ea.v_cache);
+        ok = ok && aligned16(ea.out) && (ea.ldo % 4) == 0 && (ea.d % CW) == 0 &&
+             (ea.head_dim % CW) == 0 && aligned16(ea.k_cache) && aligned16(ea.v_cache);
     }
     return ok;
 }
 
-// Epilogue of one row's 32 consecutive columns [n, n + 32), all inside the matrix, vector path.
-template <Epi E>
-__device__ __forceinline__ void epilogue32(const EpiArgs& ea, int m, int n, float* v, int M, int N,
+// Epilogue of one row's CW consecutive columns [n, n + CW), all inside the matrix, vector path.
+template <Epi E, int CW>
+__device__ __forceinline__ void epilogue_row(const EpiArgs& ea, int m, int n, float* v, int M, int N,
                                            int z, float* part, int row_map, int row_slot) {
     if (part) {
-        store32(part + static_cast<size_t>(z) * M * N + static_cast<size_t>(m) * N + n, v, true);
+        store_row<CW>(part + static_cast<size_t>(z) * M * N + static_cast<size_t>(m) * N + n, v, true);
         return;
     }
     if constexpr (E == Epi::kStore || E == Epi::kGelu) {
         if constexpr (E == Epi::kGelu) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_ref(v[j]);
+            for (int j = 0; j < CW; ++j) v[j] = gelu_ref(v[j]);
         }
-        store32(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
-        if (ea.split.planes) store_split32(v, ea.split, static_cast<size_t>(m) * ea.split.ld + n);
+        store_row<CW>(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+        if (ea.split.planes) store_split_row<CW>(v, ea.split, static_cast<size_t>(m) * ea.split.ld + n);
     } else if constexpr (E == Epi::kResidual || E == Epi::kResidualGelu) {
         const float* src = E == Epi::kResidual ? ea.out + static_cast<size_t>(m) * ea.ldo + n
                                                : ea.res + static_cast<size_t>(m) * ea.ldr + n;
-        float r[32];
+        float r[CW];
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
+        for (int j = 0; j < CW; j += 4) {
             const float4 t = *reinterpret_cast<const float4*>(src + j);
             r[j] = t.x;
             r[j + 1] = t.y;
@@ -304,13 +328,13 @@ __device__ __forceinline__ void epilogue32(const EpiArgs& ea, int m, int n, floa
             r[j + 3] = t.w;
         }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < CW; ++j) {
             v[j] = E == Epi::kResidual ? __fadd_rn(r[j], v[j]) : gelu_ref(__fadd_rn(v[j], r[j]));
         }
-        store32(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+        store_row<CW>(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
     } else if constexpr (E == Epi::kQkv) {
         if (n < ea.d) {
-            store32(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+            store_row<CW>(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
         } else {
             const int which = n / ea.d;
             const int j = n - which * ea.d;
@@ -320,22 +344,192 @@ __device__ __forceinline__ void epilogue32(const EpiArgs& ea, int m, int n, floa
                 ((static_cast<size_t>(row_map) * ea.heads + h) * ea.slots + row_slot) * ea.head_dim + e;
             void* base = which == 1 ? ea.k_cache : ea.v_cache;
             if (ea.kv_bf16) {
-                store32(static_cast<__nv_bfloat16*>(base) + idx, v, false);
+                store_row<CW>(static_cast<__nv_bfloat16*>(base) + idx, v, false);
             } else {
-                store32(static_cast<float*>(base) + idx, v, true);
+                store_row<CW>(static_cast<float*>(base) + idx, v, true);
             }
         }
     } else if constexpr (E == Epi::kLogits) {
-        store32(ea.out + static_cast<size_t>(row_map) * ea.ldo + n, v, true);
+        store_row<CW>(ea.out + static_cast<size_t>(row_map) * ea.ldo + n, v, true);
     }
 }
+
+// One tile per CTA (grid n x m x k-split): the short decode GEMMs, where every unit fits in one
+// wave. Warp 0 issues TMA, warp 1 owns TMEM and issues the MMAs, warps 2-5 drain TMEM (each warp
+// reads its 32-lane quarter) through the idle ring into row-coalesced stores. Kept apart from the
+// persistent kernel below: these launches are short, and the lean code and the single
+// accumulator measured faster here.
+constexpr int kSingleThreads = 192;
+
+// Bounded wait for the single-tile kernel (no other role to stop early).
+__device__ __forceinline__ bool mbar_wait_tile(uint64_t* bar, uint32_t parity, int* err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - start > kWaitNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+template <int FMT, int BN, Epi E>
+__global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
+    const __grid_constant__ CUtensorMap a0, const __grid_constant__ CUtensorMap a1,
+    const __grid_constant__ CUtensorMap b0, const __grid_constant__ CUtensorMap b1,
+    const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err, int splits,
+    float* __restrict__ part) {
+    using C = Config<FMT, BN>;
+    constexpr int kSingleTmemCols = BN < 32 ? 32 : BN;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + C::kStages * C::kStageBytes);
+    uint64_t* empty = full + C::kStages;
+    uint64_t* acc_full = empty + C::kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    // Split-K: this CTA accumulates k-tiles [kt0, kt1) (the host makes every split non-empty).
+    const int k_total = (K + C::kElemsPerRow - 1) / C::kElemsPerRow;
+    const int per = (k_total + splits - 1) / splits;
+    const int kt0 = blockIdx.z * per;
+    const int k_tiles = min(k_total, kt0 + per) - kt0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kSingleTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    // Set-up above touches no data of earlier kernels; operands and outputs only after the wait.
+    pdl_trigger();
+    pdl_wait();
+
+    auto stage_a = [&](int s, int p) { return base + s * C::kStageBytes + p * C::kBytesA; };
+    auto stage_b = [&](int s, int p) {
+        return base + s * C::kStageBytes + C::kPlanesA * C::kBytesA + p * C::kBytesB;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            bool ok = true;
+            for (int kt = 0; kt < k_tiles && ok; ++kt) {
+                const int s = kt % C::kStages;
+                const uint32_t phase = (kt / C::kStages) & 1;
+                ok = mbar_wait_tile(&empty[s], phase ^ 1, err, 1);
+                if (!ok) break;
+                mbar_expect_tx(&full[s], C::kStageBytes);
+                const int kx = (kt0 + kt) * C::kElemsPerRow;
+                tma_load_2d(&a0, &full[s], stage_a(s, 0), kx, m0);
+                tma_load_2d(&a1, &full[s], stage_a(s, 1), kx, m0);
+                tma_load_2d(&b0, &full[s], stage_b(s, 0), kx, n0);
+                if constexpr (C::kPlanesB == 2) tma_load_2d(&b1, &full[s], stage_b(s, 1), kx, n0);
+                ++issued;
+            }
+            if (!ok) {
+                // Drain this CTA's copies still in flight before shared memory goes away.
+                for (int kt = (issued > C::kStages ? issued - C::kStages : 0); kt < issued; ++kt) {
+                    mbar_wait_tile(&full[kt % C::kStages], (kt / C::kStages) & 1, err, 1);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = instr_desc<FMT, BN>();
+            bool ok = true;
+            for (int kt = 0; kt < k_tiles; ++kt) {
+                const int s = kt % C::kStages;
+                const uint32_t phase = (kt / C::kStages) & 1;
+                ok = mbar_wait_tile(&full[s], phase, err, 2);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                    for (int pass = 0; pass < C::kPasses; ++pass) {
+                        // tf32: (Xh,Wh), (Xh,Wl), (Xl,Wh); bf16: (Xh,W), (Xl,W).
+                        const int pa = (FMT == 2) ? (pass == 2 ? 1 : 0) : pass;
+                        const int pb = (FMT == 2) ? (pass == 1 ? 1 : 0) : 0;
+                        const uint64_t ad = smem_desc(smem_u32(stage_a(s, pa)) + kk * 32);
+                        const uint64_t bd = smem_desc(smem_u32(stage_b(s, pb)) + kk * 32);
+                        mma<FMT>(tmem, ad, bd, idesc, (kt | kk | pass) != 0);
+                    }
+                }
+                mma_commit(&empty[s]);
+            }
+            if (ok) mma_commit(acc_full);
+            else atomicCAS(err, 0, 2);
+        }
+    } else {
+        // Epilogue warps 2..5 own TMEM lane quarters (warp % 4).
+        const int quarter = warp & 3;
+        const bool ok = mbar_wait_tile(acc_full, 0, err, 3);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // Stage the 128 x BN tile through shared memory (the drained pipeline ring), so the
+        // global traffic below is row-coalesced.
+        float* tile = reinterpret_cast<float*>(base);
+        constexpr int LD = BN + 1;
+        if (__all_sync(0xffffffffu, ok)) {
+            const int r = quarter * 32 + lane;
+            const uint32_t row_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float v[16];
+                tmem_ld<16>(row_addr + c, v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) tile[r * LD + c + j] = v[j];
+            }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int t = threadIdx.x - 64;
+        if (splits > 1) {
+            float* out = part + static_cast<size_t>(blockIdx.z) * M * N;
+            for (int e = t; e < BM * BN; e += 128) {
+                const int r = e / BN, c = e - r * BN;
+                const int m = m0 + r, n = n0 + c;
+                if (m < M && n < N) out[static_cast<size_t>(m) * N + n] = tile[r * LD + c];
+            }
+        } else {
+            for (int e = t; e < BM * BN; e += 128) {
+                const int r = e / BN, c = e - r * BN;
+                const int m = m0 + r, n = n0 + c;
+                if (m < M && n < N) {
+                    const float v = tile[r * LD + c];
+                    epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, bias[n]) : v);
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kSingleTmemCols));
+    }
+}
+
 
 // Persistent tcgen05 GEMM. Work units are (n tile, m tile, k split), n fastest so that the CTAs
 // running at one time share A rows in L2; CTA b takes units b, b + gridDim.x, ... Warp 0 streams
 // k-tiles of all its units through the shared-memory ring, warp 1 issues the MMAs of unit i into
 // accumulator i % 2, and the eight epilogue warps drain the other accumulator meanwhile.
 template <int FMT, int BN, Epi E>
-__global__ __launch_bounds__(kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_tc(
+__global__ __launch_bounds__(Config<FMT, BN>::kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_tc_persistent(
     const __grid_constant__ CUtensorMap a0, const __grid_constant__ CUtensorMap a1,
     const __grid_constant__ CUtensorMap b0, const __grid_constant__ CUtensorMap b1,
     const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err, int splits,
@@ -367,16 +561,17 @@ __global__ __launch_bounds__(kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kEpiWarps);
+            mbar_init(&acc_empty[b], C::kEpiWarps);
         }
         mbar_init(drained, 1);
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    constexpr int kTmemCols = C::kTmemCols;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(C::kTmemCols));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     __syncthreads();
@@ -467,10 +662,12 @@ __global__ __launch_bounds__(kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_
             mbar_drain(drained, 0, err, 5);
         }
     } else {
-        // Epilogue warps: TMEM lane quarter warp % 4 (rows), column half (warp - 2) / 4.
+        // Epilogue warps: TMEM lane quarter warp % 4 (rows), column group (warp - 2) / 4.
+        constexpr int CW = C::CW;
+        constexpr int kSpan = BN / C::kColGroups;
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
-        const bool vec = vector_epilogue_ok<E>(ea, bias, N, splits, part);
+        const int group = (warp - 2) >> 2;
+        const bool vec = vector_epilogue_ok<E, CW>(ea, bias, N, splits, part);
         int local = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             int m0, n0, z;
@@ -490,29 +687,29 @@ __global__ __launch_bounds__(kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_
             const uint32_t row_addr =
                 tmem + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
-            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-                float v[32];
-                tmem_ld32(row_addr + c, v);
+            for (int c = group * kSpan; c < (group + 1) * kSpan; c += CW) {
+                float v[CW];
+                tmem_ld<CW>(row_addr + c, v);
                 const int n = n0 + c;
                 if (m < M && n < N) {
                 if (splits == 1 && bias) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < CW; ++j) {
                         if (n + j < N) v[j] = __fadd_rn(v[j], __ldg(bias + n + j));
                     }
                 }
-                if (vec && n + 32 <= N) {
-                    epilogue32<E>(ea, m, n, v, M, N, z, splits > 1 ? part : nullptr, row_map,
-                                  row_slot);
+                if (vec && n + CW <= N) {
+                    epilogue_row<E, CW>(ea, m, n, v, M, N, z, splits > 1 ? part : nullptr, row_map,
+                                        row_slot);
                 } else if (splits > 1) {
                     float* out = part + static_cast<size_t>(z) * M * N + static_cast<size_t>(m) * N;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < CW; ++j) {
                         if (n + j < N) out[n + j] = v[j];
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < CW; ++j) {
                         if (n + j < N) epi_apply<E>(ea, m, n + j, v[j]);
                     }
                 }
@@ -529,7 +726,7 @@ __global__ __launch_bounds__(kThreads, Config<FMT, BN>::kCtasPerSm) void k_gemm_
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(C::kTmemCols));
+                     "r"(kTmemCols));
     }
 }
 
@@ -641,9 +838,15 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
                          int N, int K, const EpiArgs& ea, int* err, const SplitK& sk) {
     using C = Config<FMT, BN>;
     const long units = static_cast<long>((N + BN - 1) / BN) * ((M + BM - 1) / BM) * sk.splits;
-    const dim3 grid(static_cast<unsigned>(std::min<long>(units, static_cast<long>(sm_count()) * C::kCtasPerSm)));
-    cudaError_t e = launch_pdl(k_gemm_tc<FMT, BN, E>, grid, dim3(kThreads), C::kSmem, s, a0, a1, b0,
-                               b1, bias, M, N, K, ea, err, sk.splits, sk.part);
+    const long resident = static_cast<long>(sm_count()) * C::kCtasPerSm;
+    const dim3 grid(static_cast<unsigned>(std::min<long>(units, resident)));  // persistent
+    cudaError_t e =
+        units > resident
+            ? launch_pdl(k_gemm_tc_persistent<FMT, BN, E>, grid, dim3(C::kThreads), C::kSmem, s, a0,
+                         a1, b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part)
+            : launch_pdl(k_gemm_tc<FMT, BN, E>,
+                         dim3((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits), dim3(kSingleThreads),
+                         C::kSmem, s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part);
     if (e != cudaSuccess || sk.splits == 1 || sk.defer) return e;
     const dim3 rgrid((N + 255) / 256, std::min(M, std::max(1, 148 * 8 / ((N + 255) / 256))));
     return launch_pdl(k_splitk_reduce<E>, rgrid, dim3(256), 0, s, sk.part, sk.splits, M, N,
@@ -673,16 +876,23 @@ cudaError_t set_smem_attrs() {
     cudaError_t err = cudaSuccess;
     for (Epi e : all) {
         const void* fn = nullptr;
-        switch (e) {
-            case Epi::kStore: fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, Epi::kStore>); break;
-            case Epi::kGelu: fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, Epi::kGelu>); break;
-            case Epi::kResidual: fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, Epi::kResidual>); break;
-            case Epi::kResidualGelu: fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, Epi::kResidualGelu>); break;
-            case Epi::kQkv: fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, Epi::kQkv>); break;
-            case Epi::kLogits: fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, Epi::kLogits>); break;
+        for (int multi = 0; multi < 2; ++multi) {
+            switch (e) {
+#define BST_GEMM_FN(EP)                                                                          \
+    fn = multi ? reinterpret_cast<const void*>(k_gemm_tc_persistent<FMT, BN, EP>)                \
+               : reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, EP>);                          \
+    break
+                case Epi::kStore: BST_GEMM_FN(Epi::kStore);
+                case Epi::kGelu: BST_GEMM_FN(Epi::kGelu);
+                case Epi::kResidual: BST_GEMM_FN(Epi::kResidual);
+                case Epi::kResidualGelu: BST_GEMM_FN(Epi::kResidualGelu);
+                case Epi::kQkv: BST_GEMM_FN(Epi::kQkv);
+                case Epi::kLogits: BST_GEMM_FN(Epi::kLogits);
+#undef BST_GEMM_FN
+            }
+            err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+            if (err != cudaSuccess) return err;
         }
-        err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-        if (err != cudaSuccess) return err;
     }
     return err;
 }
