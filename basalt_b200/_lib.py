@@ -31,7 +31,7 @@ FAMILY_LAST_TOKEN = 4
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 
-KERNEL_CLASSES = 14
+KERNEL_CLASSES = 15
 
 
 class ModelSpecStruct(ctypes.Structure):

@@ -387,6 +387,7 @@ class Engine {
     std::vector<bst::FusedLayer> fused_table;
 
     bool profiling = false;
+    bool in_step = false;  // enqueuing a batched decode step (decode_layers)
     KernelStats stats[bst::kKernelClassCount];
     std::vector<PendingTiming> pending;
     std::vector<cudaEvent_t> event_pool;
@@ -449,6 +450,7 @@ class Engine {
 
     template <typename Fn>
     cudaError_t launch(int cls, double bytes, double flops, int kernels, Fn&& fn) {
+        if (cls == bst::kGemm && in_step) cls = bst::kGemmStep;
         if (!profiling) {
             launches += kernels;
             return fn();
@@ -514,6 +516,7 @@ class Engine {
     // The layers and head of a decode step for R rows whose embedded inputs are in ws.x, on
     // `stream` (enqueue_decode runs it once, or once per lane with the workspace views shifted).
     int decode_layers(int R, const int* rowmap, const std::vector<int>& lens);
+    int qkv_partials(const LayerWeights& lw, const bst::LnArgs* ln, int R, int splits);
     int enqueue_direct(int rows);
     int prepare_fused(int rows);
     int enqueue_fused(int rows, int steps, const std::vector<int>& lens, bool history);
@@ -1187,7 +1190,38 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     return err ? cuda_fail(err, "joining the decode lanes") : BST_OK;
 }
 
+// The decode QKV projection as split-K partial sums only (no fix-up kernel): LayerNorm of ws.x
+// into the operand planes unless they already hold it (ln == nullptr), then the GEMM with
+// the fix-up deferred to the attention kernel.
+int Engine::qkv_partials(const LayerWeights& lw, const bst::LnArgs* ln, int R, int splits) {
+    const int N = 3 * d, K = d;
+    const double plane = static_cast<double>(bst::tc_split_bytes(R, K, wbf16));
+    cudaError_t err = cudaSuccess;
+    if (ln) {
+        err = launch(bst::kLayerNorm, R * K * 4.0 + 2 * plane, 0, 1, [&] {
+            return bst::launch_layernorm(stream, ws.x, d, ln->gamma, ln->beta, nullptr, 0, R, K,
+                                         ln->eps, ws.xs_hi, ws.xs_lo, wbf16 ? 2 : 1);
+        });
+        if (err) return cuda_fail(err, "qkv projection");
+    }
+    const double wbytes = static_cast<double>(N) * K * (wbf16 ? 2.0 : 8.0);
+    err = launch(bst::kGemm, wbytes + 2 * plane + static_cast<double>(splits) * R * N * 4.0,
+                 2.0 * R * N * K, 1, [&] {
+                     return bst::launch_gemm_tc(stream, ws.xs_hi, ws.xs_lo,
+                                                wbf16 ? lw.wqkv.w : lw.wqkv.hi, lw.wqkv.lo, wbf16,
+                                                lw.bqkv, R, N, K, Epi::kQkv, EpiArgs{}, ws.err,
+                                                ws.tc_part, bst::tc_part_bytes_max(), true);
+                 });
+    return err ? cuda_fail(err, "qkv projection") : BST_OK;
+}
+
 int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens) {
+    // GEMMs enqueued below are profiled as the decode step's (kGemmStep).
+    struct StepScope {
+        bool& flag;
+        explicit StepScope(bool& f) : flag(f) { flag = true; }
+        ~StepScope() { flag = false; }
+    } scope(in_step);
     const double kvb = kvbf16 ? 2.0 : 4.0;
     const int slots = ws.slots;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
@@ -1221,18 +1255,30 @@ int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens
         qkv.head_dim = hd;
         qkv.slots = slots;
         qkv.kv_bf16 = kvbf16;
-        st = x_normalised ? linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
-                                   "qkv projection", nullptr, false, true)
-                          : linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
-                                   "qkv projection", &ln1);
+        // A split-K QKV projection leaves its partial sums to the attention kernel, which sums
+        // q per head and appends the step's key and value to the cache itself.
+        bst::QkvParts qparts;
+        if (linear_on_tc(lw.wqkv, R, 3 * d, d)) {
+            const int qkv_splits = bst::tc_plan(R, 3 * d, d, wbf16, bst::tc_part_bytes_max(), nullptr);
+            if (qkv_splits > 1) qparts = bst::QkvParts{ws.tc_part, qkv_splits, lw.bqkv};
+        }
+        if (qparts.part) {
+            st = qkv_partials(lw, x_normalised ? nullptr : &ln1, R, qparts.splits);
+        } else {
+            st = x_normalised ? linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
+                                       "qkv projection", nullptr, false, true)
+                              : linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
+                                       "qkv projection", &ln1);
+        }
         if (st) return st;
-        const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0;
+        const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0 +
+                                (qparts.part ? qparts.splits * R * 3.0 * d * 4.0 : 0.0);
         const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
         st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * sum_len * d, 1, [&] {
                        return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
                                                       kvbf16, rowmap, ws.len, R, H, hd, slots,
                                                       scale, splits, chunk, ws.part,
-                                                      ws.attn_tickets, ws.att, att_planes);
+                                                      ws.attn_tickets, ws.att, att_planes, qparts);
                    }), "decode attention");
         if (st) return st;
         const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};

@@ -415,14 +415,23 @@ __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    // Set-up above touches no data of earlier kernels; operands and outputs only after the wait.
-    pdl_trigger();
-    pdl_wait();
-
     auto stage_a = [&](int s, int p) { return base + s * C::kStageBytes + p * C::kBytesA; };
     auto stage_b = [&](int s, int p) {
         return base + s * C::kStageBytes + C::kPlanesA * C::kBytesA + p * C::kBytesB;
     };
+    // Weights are constant: the first stages' weight tiles load while the previous kernel still
+    // runs. Activations (operand planes) and every output only after the wait.
+    const int pre = min(k_tiles, C::kStages);
+    if (warp == 0 && lane == 0) {
+        for (int kt = 0; kt < pre; ++kt) {
+            mbar_expect_tx(&full[kt], C::kStageBytes);
+            const int kx = (kt0 + kt) * C::kElemsPerRow;
+            tma_load_2d(&b0, &full[kt], stage_b(kt, 0), kx, n0);
+            if constexpr (C::kPlanesB == 2) tma_load_2d(&b1, &full[kt], stage_b(kt, 1), kx, n0);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -433,12 +442,14 @@ __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
                 const uint32_t phase = (kt / C::kStages) & 1;
                 ok = mbar_wait_tile(&empty[s], phase ^ 1, err, 1);
                 if (!ok) break;
-                mbar_expect_tx(&full[s], C::kStageBytes);
+                if (kt >= pre) mbar_expect_tx(&full[s], C::kStageBytes);
                 const int kx = (kt0 + kt) * C::kElemsPerRow;
                 tma_load_2d(&a0, &full[s], stage_a(s, 0), kx, m0);
                 tma_load_2d(&a1, &full[s], stage_a(s, 1), kx, m0);
-                tma_load_2d(&b0, &full[s], stage_b(s, 0), kx, n0);
-                if constexpr (C::kPlanesB == 2) tma_load_2d(&b1, &full[s], stage_b(s, 1), kx, n0);
+                if (kt >= pre) {
+                    tma_load_2d(&b0, &full[s], stage_b(s, 0), kx, n0);
+                    if constexpr (C::kPlanesB == 2) tma_load_2d(&b1, &full[s], stage_b(s, 1), kx, n0);
+                }
                 ++issued;
             }
             if (!ok) {
@@ -735,17 +746,25 @@ __global__ __launch_bounds__(Config<FMT, BN>::kThreads, Config<FMT, BN>::kCtasPe
 template <Epi E>
 __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int M, int N,
                                 const float* __restrict__ bias, EpiArgs ea) {
-    pdl_trigger();
-    pdl_wait();
     // Grid: x over column blocks of 256, y over rows (strided).
     const size_t total = static_cast<size_t>(M) * N;
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const float b = bias && n < N ? bias[n] : 0.0f;  // a weight: read before the wait
+    pdl_trigger();
+    pdl_wait();
     if (n >= N) return;
-    const float b = bias ? bias[n] : 0.0f;
     for (int m = blockIdx.y; m < M; m += gridDim.y) {
         const size_t e = static_cast<size_t>(m) * N + n;
+        // Up to 8 splits' loads in flight, then summed in split order.
+        float t[8];
+#pragma unroll
+        for (int z = 0; z < 8; ++z) t[z] = z < splits ? part[static_cast<size_t>(z) * total + e] : 0.0f;
         float v = 0.0f;
-        for (int z = 0; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
+#pragma unroll
+        for (int z = 0; z < 8; ++z) {
+            if (z < splits) v += t[z];
+        }
+        for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
         epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, b) : v);
     }
 }

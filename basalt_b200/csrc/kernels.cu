@@ -28,7 +28,7 @@ const char* kernel_class_name(int cls) {
         "embed",       "layernorm",     "gemv",          "gemm",
         "attn_decode", "attn_combine",  "attn_prefill",  "select_greedy",
         "select_sample", "gather",      "head_last_token", "misc",
-        "split",       "decode_step"};
+        "split",       "decode_step",   "gemm_step"};
     return cls >= 0 && cls < kKernelClassCount ? names[cls] : "unknown";
 }
 
@@ -406,9 +406,7 @@ __global__ __launch_bounds__(128) void k_reduce_residual_ln(
     const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
     float* __restrict__ x, int ldx, const float* __restrict__ gamma, const float* __restrict__ beta,
     float eps, void* __restrict__ hi, void* __restrict__ lo, int planes) {
-    pdl_trigger();
-    pdl_wait();
-    constexpr int ZB = 8;
+    constexpr int ZB = 16;
     __shared__ double red[4];
     __shared__ double stat;
     const int m = blockIdx.x;
@@ -416,6 +414,24 @@ __global__ __launch_bounds__(128) void k_reduce_residual_ln(
     const size_t total = static_cast<size_t>(M) * N;
     float* xr = x + static_cast<size_t>(m) * ldx;
     const float* pr = part + static_cast<size_t>(m) * N;
+    // Bias and LayerNorm parameters are weights: read before the wait, while the GEMM drains.
+    float bv[EPT], gv[EPT], tv[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        bv[j] = bias && n < N ? bias[n] : 0.0f;
+        gv[j] = n < N ? gamma[n] : 0.0f;
+        tv[j] = n < N ? beta[n] : 0.0f;
+    }
+    pdl_trigger();
+    pdl_wait();
+    // The residual row loads with the first batch of partial sums.
+    float xv[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        xv[j] = n < N ? xr[n] : 0.0f;
+    }
     float v[EPT];
 #pragma unroll
     for (int j = 0; j < EPT; ++j) v[j] = 0.0f;
@@ -442,8 +458,8 @@ __global__ __launch_bounds__(128) void k_reduce_residual_ln(
     for (int j = 0; j < EPT; ++j) {
         const int n = tid + 128 * j;
         if (n < N) {
-            const float value = bias ? __fadd_rn(v[j], bias[n]) : v[j];
-            v[j] = __fadd_rn(xr[n], value);
+            const float value = bias ? __fadd_rn(v[j], bv[j]) : v[j];
+            v[j] = __fadd_rn(xv[j], value);
             xr[n] = v[j];
         }
     }
@@ -485,7 +501,7 @@ __global__ __launch_bounds__(128) void k_reduce_residual_ln(
         if (n < N) {
             const float normalized =
                 static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(v[j]), -mean), inverse));
-            const float out = __fadd_rn(__fmul_rn(normalized, gamma[n]), beta[n]);
+            const float out = __fadd_rn(__fmul_rn(normalized, gv[j]), tv[j]);
             store_split(out, planes, hi, lo, static_cast<size_t>(m) * N + n);
         }
     }
@@ -501,7 +517,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
     const int* __restrict__ rowmap, const int* __restrict__ len, int heads, int slots,
     float scale, int splits, int chunk, float* __restrict__ part, int* __restrict__ tickets,
-    float* __restrict__ out, PlaneOut po) {
+    float* __restrict__ out, PlaneOut po, QkvParts qp) {
     constexpr int EPV = Vec16<KT>::N;
     constexpr int LPK = HD / EPV;  // lanes per key
     constexpr int KPW = 32 / LPK;  // keys per warp step
@@ -520,9 +536,54 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __shared__ float red[4 * HD];
     __shared__ float stat[8];
     __shared__ int s_last;
-    for (int e = tid; e < HD; e += 128) qs[e] = q[static_cast<size_t>(i) * d + h * HD + e];
-    __syncthreads();
     const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
+    // With the QKV partial sums, the split holding slot T - 1 (this step's own token) takes that
+    // key and value from shared memory and appends them to the cache; it never reads the slot
+    // back, so every cache read stays on the read-only path.
+    __shared__ float knew[HD], vnew[HD];
+    const bool owner = qp.part && n > 0 && end == T;
+    const int n_glob = owner ? n - 1 : n;  // keys read from the cache
+    if (qp.part) {
+        // The QKV projection's split-K fix-up for this (row, head), in split order then the
+        // bias (as k_splitk_reduce sums it).
+        const int R = gridDim.x / heads;
+        const size_t plane = static_cast<size_t>(R) * 3 * d;
+        const float* src = qp.part + static_cast<size_t>(i) * 3 * d;
+        for (int e = tid; e < (owner ? 3 : 1) * HD; e += 128) {
+            const int which = e / HD, ee = e - which * HD;
+            const int col = which * d + h * HD + ee;
+            // Up to 8 splits' loads in flight, then summed in split order.
+            float t[8];
+#pragma unroll
+            for (int z = 0; z < 8; ++z) t[z] = z < qp.splits ? __ldcg(src + z * plane + col) : 0.0f;
+            float v = 0.0f;
+#pragma unroll
+            for (int z = 0; z < 8; ++z) {
+                if (z < qp.splits) v += t[z];
+            }
+            for (int z = 8; z < qp.splits; ++z) v += __ldcg(src + z * plane + col);
+            if (qp.bias) v = __fadd_rn(v, qp.bias[col]);
+            if (which == 0) {
+                qs[ee] = v;
+            } else {
+                // The cache holds KT; attention uses the stored (rounded) value, as a read
+                // would return it.
+                KT* dst = const_cast<KT*>(which == 1 ? kc : vc) + (base + (n - 1)) * HD + ee;
+                float stored;
+                if constexpr (sizeof(KT) == 2) {
+                    *dst = __float2bfloat16_rn(v);
+                    stored = __bfloat162float(*dst);
+                } else {
+                    *dst = v;
+                    stored = v;
+                }
+                (which == 1 ? knew : vnew)[ee] = stored;
+            }
+        }
+    } else {
+        for (int e = tid; e < HD; e += 128) qs[e] = q[static_cast<size_t>(i) * d + h * HD + e];
+    }
+    __syncthreads();
     const int sub = lane % LPK, kk = lane / LPK;
     // Scores: U key groups per round, their 16-byte loads all in flight before any is used
     // (32 floats per lane).
@@ -532,8 +593,11 @@ __global__ __launch_bounds__(128) void k_attn_decode(
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int j = j0 + u * 4 * KPW + kk;
-            if (j < n) {
+            if (j < n_glob) {
                 Vec16<KT>::load(kc + (base + j) * HD + sub * EPV, kv[u]);
+            } else if (j < n) {
+#pragma unroll
+                for (int c = 0; c < EPV; ++c) kv[u][c] = knew[sub * EPV + c];
             } else {
 #pragma unroll
                 for (int c = 0; c < EPV; ++c) kv[u][c] = 0.0f;
@@ -579,9 +643,15 @@ __global__ __launch_bounds__(128) void k_attn_decode(
 #pragma unroll
         for (int u = 0; u < UV; ++u) {
             const int j = j0 + 4 * u;
-            const KT* vr = vc + (base + min(j, n - 1)) * HD + lane * DPL;
+            const int jj = min(j, n - 1);
+            if (jj < n_glob) {
+                const KT* vr = vc + (base + jj) * HD + lane * DPL;
 #pragma unroll
-            for (int c = 0; c < DPL; ++c) vv[u][c] = to_f(vr[c]);
+                for (int c = 0; c < DPL; ++c) vv[u][c] = to_f(vr[c]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < DPL; ++c) vv[u][c] = vnew[lane * DPL + c];
+            }
         }
 #pragma unroll
         for (int u = 0; u < UV; ++u) {
@@ -1077,13 +1147,13 @@ cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const floa
 
 namespace {
 template <typename KT, int HD>
-cudaError_t attn_decode_typed(cudaStream_t s, const float* q, const void* kc, const void* vc,
+cudaError_t attn_decode_typed(cudaStream_t s, const float* q, void* kc, void* vc,
                               const int* rowmap, const int* len, int R, int heads, int slots,
                               float scale, int splits, int chunk, float* part, int* tickets,
-                              float* out, const PlaneOut& po) {
+                              float* out, const PlaneOut& po, const QkvParts& qp) {
     return launch_pdl(k_attn_decode<KT, HD>, dim3(R * heads, splits), 128, 0, s, q,
                       static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len, heads,
-                      slots, scale, splits, chunk, part, tickets, out, po);
+                      slots, scale, splits, chunk, part, tickets, out, po, qp);
 }
 
 template <typename KT, int HD>
@@ -1112,16 +1182,16 @@ cudaError_t launch_reduce_residual_ln(cudaStream_t s, const float* part, int spl
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
-                               const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
-                               int R, int heads, int head_dim, int slots, float scale, int splits,
-                               int chunk, float* part, int* tickets, float* out,
-                               const PlaneOut& planes) {
+cudaError_t launch_attn_decode(cudaStream_t s, const float* q, void* k_cache, void* v_cache,
+                               int kv_bf16, const int* rowmap, const int* len, int R, int heads,
+                               int head_dim, int slots, float scale, int splits, int chunk,
+                               float* part, int* tickets, float* out, const PlaneOut& planes,
+                               const QkvParts& qkv) {
     if (R <= 0) return cudaSuccess;
     if (chunk > kMaxChunk) return cudaErrorInvalidValue;
 #define BST_ATTN_DEC(KT, HD)                                                                    \
     return attn_decode_typed<KT, HD>(s, q, k_cache, v_cache, rowmap, len, R, heads, slots,      \
-                                     scale, splits, chunk, part, tickets, out, planes)
+                                     scale, splits, chunk, part, tickets, out, planes, qkv)
     if (kv_bf16) {
         switch (head_dim) {
             case 32: BST_ATTN_DEC(__nv_bfloat16, 32);

@@ -25,7 +25,8 @@ enum KernelClass : int {
     kMisc = 11,
     kSplit = 12,
     kDecodeStep = 13,
-    kKernelClassCount = 14,
+    kGemmStep = 14,  // tensor-core GEMMs inside a batched decode step (short, weight-streaming)
+    kKernelClassCount = 15,
 };
 
 const char* kernel_class_name(int cls);
@@ -102,11 +103,21 @@ cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const floa
 // writes (unnormalised output, max, sum of exponentials) to part [R, heads, splits, head_dim + 2]
 // and the last split of each (row, head) to finish, found through tickets [R * heads] (zero
 // between launches; the kernel re-arms them), merges them in split order.
-cudaError_t launch_attn_decode(cudaStream_t s, const float* q, const void* k_cache,
-                               const void* v_cache, int kv_bf16, const int* rowmap, const int* len,
-                               int R, int heads, int head_dim, int slots, float scale, int splits,
-                               int chunk, float* part, int* tickets, float* out,
-                               const PlaneOut& planes = PlaneOut{});
+// Split-K partial sums of the QKV projection ([splits][R][3d], launch_gemm_tc with
+// defer_fixup) handed to the decode attention in place of q: each CTA sums the q of its head
+// itself (in split order, then the bias, as k_splitk_reduce does), and the CTA whose cache range
+// holds the step's own key sums that key and value and appends them to the cache.
+struct QkvParts {
+    const float* part = nullptr;
+    int splits = 0;
+    const float* bias = nullptr;
+};
+cudaError_t launch_attn_decode(cudaStream_t s, const float* q, void* k_cache, void* v_cache,
+                               int kv_bf16, const int* rowmap, const int* len, int R, int heads,
+                               int head_dim, int slots, float scale, int splits, int chunk,
+                               float* part, int* tickets, float* out,
+                               const PlaneOut& planes = PlaneOut{},
+                               const QkvParts& qkv = QkvParts{});
 // Causal prefill attention for `segments` rows; token t of segment j is packed at
 // seg_start[j] + t and sits in cache slot t of row seg_row[j].
 cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,

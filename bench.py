@@ -496,22 +496,28 @@ def main():
     top = max(prof.items(), key=lambda kv: kv[1]["ms"])
     name, k = top
     hbm, bf16, peak_src = measured_peaks()
-    per_launch_s = k["ms"] / 1000.0 / k["launches"]
-    if name in ("gemm",):
+
+    def tensor_roofline(cls, k):
+        per_launch_s = k["ms"] / 1000.0 / k["launches"]
         achieved = k["flops"] / k["launches"] / per_launch_s / 1e12
         # fp32 weights run as 3xTF32 (three tf32 passes, tf32 at half the bf16 rate); bf16
         # weights as two bf16 passes: the ceiling for useful flops is the bf16 peak over that.
         passes, rate = (2, 1.0) if m.weight_dtype == "bf16" else (3, 0.5)
         useful_peak = bf16 * rate / passes
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                    "frac": achieved / bf16, "traffic": None, "kernel": name,
-                    "peak_source": peak_src, "tensor_passes": passes,
-                    "useful_flops_peak": useful_peak, "useful_frac": achieved / useful_peak}
-    else:
+        return {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
+                "frac": achieved / bf16, "traffic": None, "kernel": cls, "peak_source": peak_src,
+                "tensor_passes": passes, "useful_flops_peak": useful_peak,
+                "useful_frac": achieved / useful_peak}
+
+    def hbm_roofline(cls, k):
+        per_launch_s = k["ms"] / 1000.0 / k["launches"]
         achieved = k["bytes"] / k["launches"] / per_launch_s / 1e9
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                    "frac": achieved / hbm, "traffic": None, "kernel": name,
-                    "peak_source": peak_src}
+        return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": None, "kernel": cls, "peak_source": peak_src}
+
+    # Prefill GEMMs ("gemm", M = prompt tokens) are tensor-bound; the decode step's GEMMs
+    # ("gemm_step", M = 128 rows per lane) stream their weights once per step: HBM / latency.
+    roofline = tensor_roofline(name, k) if name == "gemm" else hbm_roofline(name, k)
 
     line = {
         "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -532,6 +538,7 @@ def main():
                 "h2d_bytes_per_step": int(ctx.nbytes), "d2h_bytes_per_step": int(R * steps * 4)},
         "gpu_launches": int(launches),
         "roofline": roofline,
+        "roofline_prefill_gemm": tensor_roofline("gemm", prof["gemm"]) if "gemm" in prof else None,
         "kernels": kernels,
         "clocks": clocks.summary(),
     }

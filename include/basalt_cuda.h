@@ -152,7 +152,7 @@ int32_t bst_engine_stream(bst_engine engine, void** stream);
 /* Per-kernel timing, the device-side counterpart of BasaltMetrics.recordOperator
  * (BasaltMetrics.java:203-281). While enabled, each launch is bracketed by CUDA events and the
  * engine accumulates launches, device milliseconds and algorithmic bytes per kernel class. */
-#define BST_KERNEL_CLASSES 14
+#define BST_KERNEL_CLASSES 15
 int32_t bst_profile_enable(bst_engine engine, int32_t enabled);
 int32_t bst_profile_reset(bst_engine engine);
 int32_t bst_profile_read(bst_engine engine, int32_t kernel_class, char* name, int32_t capacity,
