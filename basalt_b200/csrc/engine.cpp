@@ -1099,7 +1099,8 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
                        return bst::launch_attn_prefill(stream, ws.q, qkv.k_cache, qkv.v_cache,
                                                        kvbf16, ws.seg_row, ws.seg_start,
                                                        ws.seg_len, segs, max_len, H, hd, slots,
-                                                       scale, ws.att, att_planes);
+                                                       scale, att_planes.planes ? nullptr : ws.att,
+                                                       att_planes);
                    }), "prefill attention");
         if (st) return st;
         EpiArgs res;
@@ -1110,9 +1111,9 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         if (st) return st;
         const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
         EpiArgs act;
-        act.out = ws.ffn;
         act.ldo = F;
         act.split = planes_for(lw.w2, T, d, F);
+        act.out = act.split.planes ? nullptr : ws.ffn;  // FFN2 reads only the planes
         st = linear(ws.x, d, lw.w1, lw.b1, T, F, d, Epi::kGelu, act, "ffn1", &ln2);
         if (st) return st;
         st = linear(ws.ffn, F, lw.w2, lw.b2, T, d, F, Epi::kResidual, res, "ffn2", nullptr,
@@ -1278,7 +1279,9 @@ int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens
                        return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
                                                       kvbf16, rowmap, ws.len, R, H, hd, slots,
                                                       scale, splits, chunk, ws.part,
-                                                      ws.attn_tickets, ws.att, att_planes, qparts);
+                                                      ws.attn_tickets,
+                                                      att_planes.planes ? nullptr : ws.att,
+                                                      att_planes, qparts);
                    }), "decode attention");
         if (st) return st;
         const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
@@ -1287,9 +1290,9 @@ int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens
                          "output projection", &ffn_in_normalised);
         if (st) return st;
         EpiArgs act;
-        act.out = ws.ffn;
         act.ldo = F;
         act.split = planes_for(lw.w2, R, d, F);
+        act.out = act.split.planes ? nullptr : ws.ffn;  // FFN2 reads only the planes
         st = ffn_in_normalised ? linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
                                         nullptr, false, true)
                                : linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",

@@ -40,7 +40,7 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float
         }
     } else if constexpr (E == Epi::kGelu) {
         const float g = gelu_ref(v);
-        ea.out[static_cast<size_t>(m) * ea.ldo + n] = g;
+        if (ea.out) ea.out[static_cast<size_t>(m) * ea.ldo + n] = g;
         if (ea.split.planes) {
             store_split(g, ea.split.planes, ea.split.hi, ea.split.lo, static_cast<size_t>(m) * ea.split.ld + n);
         }

@@ -313,7 +313,7 @@ __device__ __forceinline__ void epilogue_row(const EpiArgs& ea, int m, int n, fl
 #pragma unroll
             for (int j = 0; j < CW; ++j) v[j] = gelu_ref(v[j]);
         }
-        store_row<CW>(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
+        if (ea.out) store_row<CW>(ea.out + static_cast<size_t>(m) * ea.ldo + n, v, true);
         if (ea.split.planes) store_split_row<CW>(v, ea.split, static_cast<size_t>(m) * ea.split.ld + n);
     } else if constexpr (E == Epi::kResidual || E == Epi::kResidualGelu) {
         const float* src = E == Epi::kResidual ? ea.out + static_cast<size_t>(m) * ea.ldo + n

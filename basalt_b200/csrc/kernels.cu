@@ -398,9 +398,10 @@ __global__ __launch_bounds__(256) void k_layernorm(const float* __restrict__ x, 
 
 // Split-K fix-up of a residual projection, then the LayerNorm of the updated rows into operand
 // planes (see launch_reduce_residual_ln). One CTA of 128 threads per row; a thread owns EPT
-// columns (n = tid + 128 j) and loads their partials of up to 8 splits at once. The splits are
-// summed in order as k_splitk_reduce does; the f64 statistics are k_layernorm's up to the order
-// of the f64 additions.
+// columns (n = tid + 128 j) and loads their partials of up to 16 splits at once, together with
+// the residual row (bias, gamma and beta are read before the PDL wait). The splits are summed in
+// order as k_splitk_reduce does; the f64 statistics are k_layernorm's up to the order of the f64
+// additions.
 template <int EPT>
 __global__ __launch_bounds__(128) void k_reduce_residual_ln(
     const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
@@ -668,7 +669,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
         for (int e = tid; e < HD; e += 128) {
             const float acc = red[e] + red[HD + e] + red[2 * HD + e] + red[3 * HD + e];
             const size_t at = static_cast<size_t>(i) * d + h * HD + e;
-            out[at] = acc / sum;
+            if (out) out[at] = acc / sum;
             if (po.planes) store_split(acc / sum, po.planes, po.hi, po.lo, at);
         }
         return;
@@ -700,7 +701,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
             O = fmaf(__ldcg(all + z * (HD + 2) + e), wgt, O);
         }
         const size_t at = static_cast<size_t>(i) * d + h * HD + e;
-        out[at] = O / L;
+        if (out) out[at] = O / L;
         if (po.planes) store_split(O / L, po.planes, po.hi, po.lo, at);
     }
     if (tid == 0) tickets[i * heads + h] = 0;
@@ -888,7 +889,7 @@ __global__ __launch_bounds__(256, HD > 64 ? 2 : 3) void k_attn_prefill(
         for (int c = 0; c < OC; ++c) {
             const int col = HD == 32 ? 2 * tx + c : 64 * (c / 4) + 4 * tx + (c % 4);
             const float v = o[i][c] / l[i];
-            dst[col] = v;
+            if (out) dst[col] = v;
             if (po.planes) store_split(v, po.planes, po.hi, po.lo, at0 + col);
         }
     }

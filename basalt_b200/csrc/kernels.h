@@ -119,7 +119,8 @@ cudaError_t launch_attn_decode(cudaStream_t s, const float* q, void* k_cache, vo
                                const PlaneOut& planes = PlaneOut{},
                                const QkvParts& qkv = QkvParts{});
 // Causal prefill attention for `segments` rows; token t of segment j is packed at
-// seg_start[j] + t and sits in cache slot t of row seg_row[j].
+// seg_start[j] + t and sits in cache slot t of row seg_row[j]. In both attention kernels `out`
+// may be null when `planes` receives the result (the O projection reads only the planes).
 cudaError_t launch_attn_prefill(cudaStream_t s, const float* q, const void* k_cache,
                                 const void* v_cache, int kv_bf16, const int* seg_row,
                                 const int* seg_start, const int* seg_len, int segments,
