@@ -193,18 +193,20 @@ struct Config {
     static constexpr int kBytesA = kTileRowsA * kRowBytes;  // one plane
     static constexpr int kBytesB = BN * kRowBytes;
     static constexpr int kStageBytes = kPlanesA * kBytesA + kPlanesB * kBytesB;
-    // Narrow tiles serve the short decode GEMMs: two stages (<= 96 KB) let two CTAs share an SM.
-    static constexpr int kStages = BN == 64 ? 2 : (192 * 1024) / kStageBytes;
+    // Narrow tiles serve the short decode GEMMs: three stages (<= 144 KB). Measured on the
+    // two-lane decode step: 2 stages (two CTAs per SM) and 4 stages (192 KB, little room left
+    // for the other lane's kernels on the SM) were both ~4-5 % slower.
+    static constexpr int kStages = BN == 64 ? 3 : (192 * 1024) / kStageBytes;
     static constexpr int kElemsPerRow = FMT == 2 ? 32 : 64;  // K per stage
     static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
     // Two accumulators for the persistent variant: the epilogue drains one while the MMAs fill
     // the other.
     static constexpr int kTmemCols = 2 * BN;
-    static constexpr int kCtasPerSm = BN == 64 ? 2 : 1;
+    static constexpr int kCtasPerSm = kStages * kStageBytes <= 100 * 1024 ? 2 : 1;
     // Epilogue warps 2.. cover the four TMEM lane quarters kColGroups times over, each warp a
     // column range of BN / kColGroups drained CW columns at a time. The narrow decode tiles keep
-    // a small footprint (192 threads, 16-column chunks) so that two CTAs and the other decode
-    // lane's kernels share an SM.
+    // a small footprint (192 threads, 16-column chunks) so that the other decode lane's kernels
+    // share the SM.
     static constexpr int kColGroups = BN == 64 ? 1 : 2;
     static constexpr int kEpiWarps = 4 * kColGroups;
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
