@@ -185,7 +185,7 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v) {
     for (int i = 0; i < CW; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int FMT, int BN>
+template <int FMT, int BN, int ST = 0>
 struct Config {
     static constexpr int kPlanesA = 2;
     static constexpr int kPlanesB = FMT == 2 ? 2 : 1;
@@ -193,10 +193,12 @@ struct Config {
     static constexpr int kBytesA = kTileRowsA * kRowBytes;  // one plane
     static constexpr int kBytesB = BN * kRowBytes;
     static constexpr int kStageBytes = kPlanesA * kBytesA + kPlanesB * kBytesB;
-    // Narrow tiles serve the short decode GEMMs: three stages (<= 144 KB). Measured on the
-    // two-lane decode step: 2 stages (two CTAs per SM) and 4 stages (192 KB, little room left
-    // for the other lane's kernels on the SM) were both ~4-5 % slower.
-    static constexpr int kStages = BN == 64 ? 3 : (192 * 1024) / kStageBytes;
+    // Narrow tiles serve the short decode GEMMs: three stages (<= 144 KB, one CTA per SM) when
+    // the units fit one wave of the SMs. Measured on the two-lane decode step of 128-row lanes:
+    // 2 stages (two CTAs per SM) and 4 stages (192 KB, little room left for the other lane's
+    // kernels on the SM) were both ~4-5 % slower. GEMMs with up to two units per SM (512-row
+    // lanes) run the ST = 2 variant, two CTAs per SM, in one wave.
+    static constexpr int kStages = ST ? ST : BN == 64 ? 3 : (192 * 1024) / kStageBytes;
     static constexpr int kElemsPerRow = FMT == 2 ? 32 : 64;  // K per stage
     static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
     // Two accumulators for the persistent variant: the epilogue drains one while the MMAs fill
@@ -376,13 +378,13 @@ __device__ __forceinline__ bool mbar_wait_tile(uint64_t* bar, uint32_t parity, i
     return true;
 }
 
-template <int FMT, int BN, Epi E>
+template <int FMT, int BN, Epi E, int ST>
 __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
     const __grid_constant__ CUtensorMap a0, const __grid_constant__ CUtensorMap a1,
     const __grid_constant__ CUtensorMap b0, const __grid_constant__ CUtensorMap b1,
     const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err, int splits,
     float* __restrict__ part) {
-    using C = Config<FMT, BN>;
+    using C = Config<FMT, BN, ST>;
     constexpr int kSingleTmemCols = BN < 32 ? 32 : BN;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -859,15 +861,24 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
                          int N, int K, const EpiArgs& ea, int* err, const SplitK& sk) {
     using C = Config<FMT, BN>;
     const long units = static_cast<long>((N + BN - 1) / BN) * ((M + BM - 1) / BM) * sk.splits;
-    const long resident = static_cast<long>(sm_count()) * C::kCtasPerSm;
-    const dim3 grid(static_cast<unsigned>(std::min<long>(units, resident)));  // persistent
-    cudaError_t e =
-        units > resident
-            ? launch_pdl(k_gemm_tc_persistent<FMT, BN, E>, grid, dim3(C::kThreads), C::kSmem, s, a0,
-                         a1, b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part)
-            : launch_pdl(k_gemm_tc<FMT, BN, E>,
-                         dim3((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits), dim3(kSingleThreads),
-                         C::kSmem, s, a0, a1, b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part);
+    const long sms = sm_count();
+    const long resident = sms * C::kCtasPerSm;
+    const dim3 tiles((N + BN - 1) / BN, (M + BM - 1) / BM, sk.splits);
+    cudaError_t e = cudaSuccess;
+    if (units <= resident) {
+        e = launch_pdl(k_gemm_tc<FMT, BN, E, 0>, tiles, dim3(kSingleThreads), C::kSmem, s, a0, a1,
+                       b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part);
+    } else if (BN == 64 && units <= sms * Config<FMT, BN, 2>::kCtasPerSm) {
+        if constexpr (BN == 64) {
+            e = launch_pdl(k_gemm_tc<FMT, BN, E, 2>, tiles, dim3(kSingleThreads),
+                           Config<FMT, BN, 2>::kSmem, s, a0, a1, b0, b1, bias, M, N, K, ea, err,
+                           sk.splits, sk.part);
+        }
+    } else {
+        const dim3 grid(static_cast<unsigned>(std::min<long>(units, resident)));
+        e = launch_pdl(k_gemm_tc_persistent<FMT, BN, E>, grid, dim3(C::kThreads), C::kSmem, s, a0,
+                       a1, b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part);
+    }
     if (e != cudaSuccess || sk.splits == 1 || sk.defer) return e;
     const dim3 rgrid((N + 255) / 256, std::min(M, std::max(1, 148 * 8 / ((N + 255) / 256))));
     return launch_pdl(k_splitk_reduce<E>, rgrid, dim3(256), 0, s, sk.part, sk.splits, M, N,
@@ -897,11 +908,17 @@ cudaError_t set_smem_attrs() {
     cudaError_t err = cudaSuccess;
     for (Epi e : all) {
         const void* fn = nullptr;
-        for (int multi = 0; multi < 2; ++multi) {
+        for (int variant = 0; variant < (BN == 64 ? 3 : 2); ++variant) {
+            int smem = C::kSmem;
             switch (e) {
 #define BST_GEMM_FN(EP)                                                                          \
-    fn = multi ? reinterpret_cast<const void*>(k_gemm_tc_persistent<FMT, BN, EP>)                \
-               : reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, EP>);                          \
+    if (variant == 2) {                                                                          \
+        fn = reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, EP, BN == 64 ? 2 : 0>);            \
+        smem = Config<FMT, BN, BN == 64 ? 2 : 0>::kSmem;                                         \
+    } else {                                                                                     \
+        fn = variant ? reinterpret_cast<const void*>(k_gemm_tc_persistent<FMT, BN, EP>)          \
+                     : reinterpret_cast<const void*>(k_gemm_tc<FMT, BN, EP, 0>);                 \
+    }                                                                                            \
     break
                 case Epi::kStore: BST_GEMM_FN(Epi::kStore);
                 case Epi::kGelu: BST_GEMM_FN(Epi::kGelu);
@@ -911,7 +928,7 @@ cudaError_t set_smem_attrs() {
                 case Epi::kLogits: BST_GEMM_FN(Epi::kLogits);
 #undef BST_GEMM_FN
             }
-            err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+            err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (err != cudaSuccess) return err;
         }
     }

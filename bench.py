@@ -292,16 +292,18 @@ def other_configs(local, reps=3):
             else:
                 engine.generate_device(d_ctx.data_ptr(), w.rows, ctx.shape[1], n, dst.data_ptr())
 
-        n_reps = 1 if w.rows > 4096 else reps
-
         def timed(n, dst):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            for _ in range(n_reps):
+            # Median of separately timed calls: the decode figure is a difference of two call
+            # times, so one slow call would otherwise move it a lot.
+            times = []
+            for _ in range(reps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
                 call(n, dst)
-            b.record(stream)
-            b.synchronize()
-            return a.elapsed_time(b) / n_reps
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            return float(np.median(times))
 
         call(w.steps, d_tok)
         call(1, d_one)
