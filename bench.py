@@ -161,6 +161,16 @@ def cpu_baseline(workload, weights_path, threads=None, budget_s=15.0):
     return line
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of a kernel class, from one
+# ncu capture of the named workload (the commands are kept with the profile summaries):
+# "gemm_step": mean over the 25 projection launches of one lane's decode step (at ~258 cached
+# keys); "gemm": mean over the four prefill projections of one layer (M = 65 536 tokens).
+NCU_TRAFFIC = {
+    ("v4096-d512-l6-w512-b256-greedy", "gemm_step"): 7.64e6,
+    ("v4096-d512-l6-w512-b256-greedy", "gemm"): 0.956e9,
+}
+
+
 def profile_summary(engine, run):
     """Per-kernel device time of one call of `run`, CUDA events around every launch."""
     import torch
@@ -520,6 +530,7 @@ def main():
     # Prefill GEMMs ("gemm", M = prompt tokens) are tensor-bound; the decode step's GEMMs
     # ("gemm_step", M = 128 rows per lane) stream their weights once per step: HBM / latency.
     roofline = tensor_roofline(name, k) if name == "gemm" else hbm_roofline(name, k)
+    roofline["traffic"] = NCU_TRAFFIC.get((workload.name, name))
 
     line = {
         "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -540,7 +551,9 @@ def main():
                 "h2d_bytes_per_step": int(ctx.nbytes), "d2h_bytes_per_step": int(R * steps * 4)},
         "gpu_launches": int(launches),
         "roofline": roofline,
-        "roofline_prefill_gemm": tensor_roofline("gemm", prof["gemm"]) if "gemm" in prof else None,
+        "roofline_prefill_gemm": (
+            {**tensor_roofline("gemm", prof["gemm"]),
+             "traffic": NCU_TRAFFIC.get((workload.name, "gemm"))} if "gemm" in prof else None),
         "kernels": kernels,
         "clocks": clocks.summary(),
     }
