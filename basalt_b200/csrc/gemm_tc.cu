@@ -969,14 +969,15 @@ cudaError_t launch_split_operand(cudaStream_t s, const float* x, int ldx, int M,
 
 int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out) {
     // Narrow tiles when the grid would not cover the SMs, then split K until it does (one wave);
-    // each split keeps at least two k-tiles.
+    // each split keeps at least four k-tiles (measured on the decode step against two, six and
+    // eight: fewer partials to sum beats the shorter split GEMMs up to that point).
     const int tiles_m = (M + BM - 1) / BM;
     const int bn = ((N + 127) / 128) * tiles_m >= 148 ? 128 : 64;
     const int tiles = ((N + bn - 1) / bn) * tiles_m;
     const int k_tiles = (K + (w_bf16 ? 63 : 31)) / (w_bf16 ? 64 : 32);
     int splits = 1;
     if (tiles < 148) {
-        splits = std::min((148 + tiles - 1) / tiles, std::max(1, k_tiles / 2));
+        splits = std::min((148 + tiles - 1) / tiles, std::max(1, k_tiles / 4));
         const size_t per_split = static_cast<size_t>(M) * N * sizeof(float);
         while (splits > 1 && per_split * splits > part_bytes) --splits;
         if (splits > 1) {
