@@ -359,10 +359,11 @@ __device__ __forceinline__ void epilogue_row(const EpiArgs& ea, int m, int n, fl
 }
 
 // One tile per CTA (grid n x m x k-split): the short decode GEMMs, where every unit fits in one
-// wave. Warp 0 issues TMA, warp 1 owns TMEM and issues the MMAs, warps 2-5 drain TMEM (each warp
-// reads its 32-lane quarter) through the idle ring into row-coalesced stores. Kept apart from the
-// persistent kernel below: these launches are short, and the lean code and the single
-// accumulator measured faster here.
+// wave. Warp 0 issues TMA (the weight tiles of the first stages before the PDL wait), warp 1 owns
+// TMEM and issues the MMAs, warps 2-5 drain TMEM (each warp reads its 32-lane quarter) through
+// the idle ring into row-coalesced stores. ST overrides the ring depth (0: Config's default, one
+// CTA per SM for narrow tiles; 2: two CTAs per SM). Kept apart from the persistent kernel below:
+// these launches are short, and the lean code and the single accumulator measured faster here.
 constexpr int kSingleThreads = 192;
 
 // Bounded wait for the single-tile kernel (no other role to stop early).
