@@ -97,3 +97,20 @@ def test_v8192_d768_l12_sampled_rows_of_the_8192_sequence_run(runtime, tmp_path)
         ref = oracle.scores(window_at(ctx[r], tokens[r], g, W))
         want, margin, _ = draw_margin(ref, w.temperature, w.k, state)
         assert want == tokens[r, g] or margin < 1e-4, (r, g, tokens[r, g], want)
+
+
+def test_v8192_d768_l12_512_rows_greedy_bf16_weights(runtime, tmp_path):
+    # 512 rows (two lanes of 256) of the 8192-sequence run's architecture: its decode projections
+    # have between one and two work units per SM (e.g. the QKV GEMM: 72 tiles x 3 splits), the
+    # case served by the two-CTAs-per-SM ring of the one-tile GEMM.
+    from dataclasses import replace
+
+    w = config("v8192-d768-l12-w1024-n8192-sampled-bf16w")
+    m = replace(w.model, max_rows=0)
+    w = replace(w, model=m, rows=512, steps=4, mode="greedy")
+    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
+    W, V = m.window, m.vocabulary
+    ctx = left_pad(synthetic_prompts(w.prompt_seed, 512, w.prompt, V), W, V)
+    tokens = engine.generateBatch(ctx, w.steps)
+    assert tokens.shape == (512, 4) and tokens.min() >= 0 and tokens.max() < V
+    check_points(engine, oracle, ctx, tokens, [(0, 0), (300, 3), (511, 3)], W)
