@@ -47,23 +47,26 @@ def test_char_lm_rejects_ids_outside_the_vocabulary(runtime, tmp_path):
         engine.generate([1, 2, 3, 30], 1)
 
 
-def test_bf16_kv_cache_holds_a_stated_tolerance(runtime, tmp_path):
+@pytest.mark.parametrize("rows", [4, 24])
+def test_bf16_kv_cache_holds_a_stated_tolerance(runtime, tmp_path, rows):
     # KV stored in bf16 (8 mantissa bits) against the fp32 oracle: logits within 2e-2, tokens
-    # identical except where the oracle's top-2 gap is below that tolerance.
+    # identical except where the oracle's top-2 gap is below that tolerance. 4 rows run the fused
+    # decode step; 24 rows the batched step, where the QKV projection is split-K and the decode
+    # attention sums it and appends the (bf16-rounded) key and value itself.
     tol = 2e-2
     spec = ModelSpec("padded_decoder", 512, 96, 256, 3, 4, 768, kv_dtype="bf16")
     engine, oracle = pair(runtime, spec, tmp_path / "w.bin")
-    ctx = left_pad(synthetic_prompts(8, 4, 40, 512), 96, 512)
+    ctx = left_pad(synthetic_prompts(8, rows, 40, 512), 96, 512)
     tokens, logits = engine.generateWithLogits(ctx, 40)
     mismatched = 0
-    for r in range(4):
+    for r in range(rows):
         ref = oracle.forced_scores(ctx[r], tokens[r])
         compare_logits(logits[r], ref, atol=tol, rtol=0, where=f"row{r}")
         for step in range(40):
             if int(np.argmax(ref[step])) != tokens[r, step]:
                 assert top2_gap(ref[step]) < tol
                 mismatched += 1
-    assert mismatched <= 4
+    assert mismatched <= rows
 
 
 def test_waves_sample_exactly_like_one_batch(runtime, tmp_path):
