@@ -220,13 +220,17 @@ def batch1(local, steps, warmup):
     torch.cuda.synchronize()
 
     def timed(n, out, reps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
+        # Median of separately timed calls: the per-token figure is a difference of two call
+        # times, so one slow call would otherwise move it a lot.
+        times = []
+        for _ in range(max(3, reps)):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
             call(n, out)
-        b.record(stream)
-        b.synchronize()
-        return a.elapsed_time(b) / reps
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        return float(np.median(times))
 
     full_ms = timed(w.steps, d_tok, steps)
     prefill_ms = timed(1, d_one, steps)
