@@ -508,6 +508,66 @@ __global__ __launch_bounds__(128) void k_reduce_residual_ln(
     }
 }
 
+
+// Streaming loads for the decode attention's K/V: read once per step, so they are marked
+// evict-first in L2 (the projections' weights and split-K partials stay resident instead).
+__device__ __forceinline__ unsigned long long evict_first_policy() {
+    unsigned long long pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void load16_stream(const float* p, float* out, unsigned long long pol) {
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(out[0]), "=f"(out[1]), "=f"(out[2]), "=f"(out[3])
+                 : "l"(p), "l"(pol));
+}
+__device__ __forceinline__ void load16_stream(const __nv_bfloat16* p, float* out,
+                                              unsigned long long pol) {
+    uint32_t w[4];
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.b32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                 : "l"(p), "l"(pol));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        out[2 * i] = bf16_bits_to_f(w[i] & 0xffffu);
+        out[2 * i + 1] = bf16_bits_to_f(w[i] >> 16);
+    }
+}
+// DPL consecutive values (DPL = 1, 2 or 4) of a V row, streaming.
+template <int DPL>
+__device__ __forceinline__ void load_row_stream(const float* p, float* out, unsigned long long pol) {
+    if constexpr (DPL == 4) {
+        load16_stream(p, out, pol);
+    } else if constexpr (DPL == 2) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
+                     : "=f"(out[0]), "=f"(out[1]) : "l"(p), "l"(pol));
+    } else {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;"
+                     : "=f"(out[0]) : "l"(p), "l"(pol));
+    }
+}
+template <int DPL>
+__device__ __forceinline__ void load_row_stream(const __nv_bfloat16* p, float* out,
+                                                unsigned long long pol) {
+    if constexpr (DPL == 4) {
+        uint32_t w[2];
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.b32 {%0, %1}, [%2], %3;"
+                     : "=r"(w[0]), "=r"(w[1]) : "l"(p), "l"(pol));
+        out[0] = bf16_bits_to_f(w[0] & 0xffffu); out[1] = bf16_bits_to_f(w[0] >> 16);
+        out[2] = bf16_bits_to_f(w[1] & 0xffffu); out[3] = bf16_bits_to_f(w[1] >> 16);
+    } else if constexpr (DPL == 2) {
+        uint32_t w;
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.b32 %0, [%1], %2;"
+                     : "=r"(w) : "l"(p), "l"(pol));
+        out[0] = bf16_bits_to_f(w & 0xffffu); out[1] = bf16_bits_to_f(w >> 16);
+    } else {
+        unsigned short h;
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.b16 %0, [%1], %2;"
+                     : "=h"(h) : "l"(p), "l"(pol));
+        out[0] = bf16_bits_to_f(h);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Decode attention, split over the cached keys. One CTA per (row, head, split); writes the
 // split's running max, sum of exponentials and unnormalised output. Scores follow
@@ -538,6 +598,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __shared__ float stat[8];
     __shared__ int s_last;
     const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
+    const unsigned long long pol = evict_first_policy();
     // With the QKV partial sums, the split holding slot T - 1 (this step's own token) takes that
     // key and value from shared memory and appends them to the cache; it never reads the slot
     // back, so every cache read stays on the read-only path.
@@ -595,7 +656,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
         for (int u = 0; u < U; ++u) {
             const int j = j0 + u * 4 * KPW + kk;
             if (j < n_glob) {
-                Vec16<KT>::load(kc + (base + j) * HD + sub * EPV, kv[u]);
+                load16_stream(kc + (base + j) * HD + sub * EPV, kv[u], pol);
             } else if (j < n) {
 #pragma unroll
                 for (int c = 0; c < EPV; ++c) kv[u][c] = knew[sub * EPV + c];
@@ -646,9 +707,7 @@ __global__ __launch_bounds__(128) void k_attn_decode(
             const int j = j0 + 4 * u;
             const int jj = min(j, n - 1);
             if (jj < n_glob) {
-                const KT* vr = vc + (base + jj) * HD + lane * DPL;
-#pragma unroll
-                for (int c = 0; c < DPL; ++c) vv[u][c] = to_f(vr[c]);
+                load_row_stream<DPL>(vc + (base + jj) * HD + lane * DPL, vv[u], pol);
             } else {
 #pragma unroll
                 for (int c = 0; c < DPL; ++c) vv[u][c] = vnew[lane * DPL + c];
