@@ -76,6 +76,12 @@ SIGNATURES = {
     "bst_sample_logits": (ctypes.c_int32, [_u64, _i32p, ctypes.c_int32, ctypes.c_int32,
                                            ctypes.c_int32, ctypes.c_float, ctypes.c_int32, _i32p,
                                            _f32p]),
+    "bst_generate_logits_rows": (ctypes.c_int32, [_u64, _i32p, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_int32, _i32p, ctypes.c_int32, _i32p,
+                                                  _f32p]),
+    "bst_sample_logits_rows": (ctypes.c_int32, [_u64, _i32p, ctypes.c_int32, ctypes.c_int32,
+                                                ctypes.c_int32, ctypes.c_float, ctypes.c_int32,
+                                                _i32p, ctypes.c_int32, _i32p, _f32p]),
     "bst_generate_device": (ctypes.c_int32, [_u64, ctypes.c_void_p, ctypes.c_int32,
                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "bst_sample_device": (ctypes.c_int32, [_u64, ctypes.c_void_p, ctypes.c_int32,

@@ -11,7 +11,8 @@
 // overlaps the barrier and the input staging.
 //
 // Phases (R <= 8 rows, every row extending its cache; TransformerBlock.forward,
-// TransformerBlock.java:40-52, and TransformerLanguageModel.forward, zoo/Zoo.java:100-133):
+// torch/TransformerBlock.java:37-43, inside the padded decoder whose last-position head follows
+// TextEngine.scores, infer/TextEngine.java:96-112):
 //   embed      every CTA computes x[i] = tok[next[i]] + pos[len[i]] itself (no barrier)
 //   per layer  QKV (LN1 fused; K/V stored at slot len[i]) | attention (one warp per 32-key
 //              chunk; the last chunk of a (row, head) merges the chunk partials in chunk order) |
@@ -742,6 +743,10 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
     __shared__ int abort_flag, s_len[kMaxRows], s_next[kMaxRows], s_rows[kMaxRows], s_step, s_last;
     __shared__ unsigned long long s_best[kMaxRows];
     __shared__ __align__(8) uint64_t s_wbar;
+    // After a timed-out barrier or weight stage in an earlier step of the run, the barrier count
+    // no longer matches what this launch expects: return at once (the host reports the error
+    // recorded in *err once the run's queued steps have drained).
+    if (__ldcg(p.err) != 0) return;
     const int R = p.R, d = p.d, F = p.F;
     int dc0, dc1;
     column_block(d, &dc0, &dc1);

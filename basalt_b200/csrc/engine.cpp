@@ -313,7 +313,8 @@ struct Workspace {
     int* attn_tickets = nullptr;  // decode-attention split merge tickets [rows * heads]
     float *flat = nullptr, *mixed = nullptr;  // charLm
     float* history = nullptr;                 // per-step logits, when requested
-    bool has_history = false;
+    int* hist_rows_of = nullptr;              // history row h holds the logits of this wave row
+    size_t hist_capacity = 0;                 // floats the history buffer holds
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
     void *ys_hi = nullptr, *ys_lo = nullptr;  // planes a producer writes for the next projection
     // The second decode lane's operand planes ([rows][max(d, F)]) and split-K partials.
@@ -383,6 +384,10 @@ class Engine {
     std::string graph_key;
     int64_t graph_nodes = 0;
     int fused_rows = 0, fused_ctas = 0;  // shape the fused decode step was prepared for
+    // Rows (global indices, in output order) whose logits a *_logits_rows call returns; empty:
+    // every row. hist_count: rows of the current wave whose logits are stashed.
+    std::vector<int32_t> watch;
+    int hist_count = 0;
     unsigned fused_bar_base = 0;         // the fused step's barrier count on the device
     std::vector<bst::FusedLayer> fused_table;
 
@@ -482,7 +487,8 @@ class Engine {
 
     // ---- parameters ----
     int upload_weights();
-    int ensure_workspace(int rows, int steps, int slots, int tokens, int splits, bool history);
+    // hist_rows: rows whose per-step logits this run keeps (0: none).
+    int ensure_workspace(int rows, int steps, int slots, int tokens, int splits, int hist_rows);
     void free_workspace();
 
     // ---- runs ----
@@ -523,6 +529,13 @@ class Engine {
     int enqueue_select(Mode mode, int rows, int steps, float temperature, int top_k,
                        bool history);
 };
+
+// Message for an error code a kernel recorded in the workspace's status word.
+std::string pipeline_message(int code) {
+    if (code == 11) return "a grid barrier of the fused decode step timed out";
+    if (code == 12) return "the fused decode step's weight staging (TMA bulk copy) timed out";
+    return "a tensor-core GEMM pipeline wait timed out (stage " + std::to_string(code) + ")";
+}
 
 std::mutex g_registry_mutex;
 std::unordered_map<uint64_t, std::shared_ptr<Engine>> g_engines;
@@ -749,9 +762,10 @@ void Engine::free_workspace() {
 }
 
 int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int splits,
-                             bool history) {
+                             int hist_rows) {
+    const size_t hist_floats = static_cast<size_t>(hist_rows) * steps * V;
     if (ws.arena.ptr && ws.rows >= rows && ws.steps >= steps && ws.slots == slots &&
-        ws.tokens >= tokens && ws.splits >= splits && (ws.has_history || !history)) {
+        ws.tokens >= tokens && ws.splits >= splits && ws.hist_capacity >= hist_floats) {
         return BST_OK;
     }
     free_workspace();
@@ -796,9 +810,9 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     }
     add(reinterpret_cast<void**>(&ws.rng), sizeof(uint64_t) * rows);
     add(reinterpret_cast<void**>(&ws.logits), sizeof(float) * static_cast<size_t>(rows) * V);
-    if (history) {
-        add(reinterpret_cast<void**>(&ws.history),
-            sizeof(float) * static_cast<size_t>(rows) * steps * V);
+    if (hist_floats) {
+        add(reinterpret_cast<void**>(&ws.history), sizeof(float) * hist_floats);
+        add(reinterpret_cast<void**>(&ws.hist_rows_of), sizeof(int) * rows);
     }
     if (decoder_family(spec.family)) {
         add(reinterpret_cast<void**>(&ws.seg_row), sizeof(int) * rows);
@@ -848,7 +862,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     ws.slots = slots;
     ws.tokens = tokens;
     ws.splits = splits;
-    ws.has_history = history;
+    ws.hist_capacity = hist_floats;
     ws.generation = next_generation++;
     err = bst::launch_iota(stream, ws.rowmap_all, rows);
     if (!err && ws.attn_tickets) {
@@ -1458,7 +1472,8 @@ int Engine::enqueue_select(Mode mode, int rows, int steps, float temperature, in
     cudaError_t err;
     if (history) {
         err = launch(bst::kMisc, rows * V * 8.0, 0, 1, [&] {
-            return bst::launch_stash_logits(stream, ws.logits, rows, V, steps, ws.step, ws.history);
+            return bst::launch_stash_logits(stream, ws.logits, hist_count, V, steps, ws.step,
+                                            ws.hist_rows_of, ws.history);
         });
         if (err) return cuda_fail(err, "stashing logits");
     }
@@ -1481,8 +1496,36 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
                      int steps, float temperature, int top_k, uint64_t rng_base, int32_t* tokens,
                      bool tokens_on_device, int total_rows, bst_token_sink sink, void* user,
                      double* scores, float* logits) {
-    const bool history = logits != nullptr && mode != Mode::kScores;
     const int run_steps = mode == Mode::kScores ? 1 : steps;
+    // Rows of this wave whose per-step logits are kept (hist_local) and the output slot of each
+    // (-1: kept only because the fused step writes every row's logits).
+    std::vector<int> hist_local, hist_out;
+    if (logits != nullptr && mode != Mode::kScores) {
+        for (int r = 0; r < rows; ++r) {
+            if (watch.empty()) {
+                hist_local.push_back(r);
+                hist_out.push_back(row0 + r);
+                continue;
+            }
+            for (size_t i = 0; i < watch.size(); ++i) {
+                if (watch[i] == row0 + r) {
+                    hist_local.push_back(r);
+                    hist_out.push_back(static_cast<int>(i));
+                    break;
+                }
+            }
+        }
+        if (!hist_local.empty() && mode == Mode::kGreedy && rows <= 8 &&
+            static_cast<int>(hist_local.size()) != rows) {
+            std::vector<int> out(rows, -1);
+            for (size_t i = 0; i < hist_local.size(); ++i) out[hist_local[i]] = hist_out[i];
+            hist_local.resize(rows);
+            for (int r = 0; r < rows; ++r) hist_local[r] = r;
+            hist_out = out;
+        }
+    }
+    const bool history = !hist_local.empty();
+    const int hist_rows = static_cast<int>(hist_local.size());
     std::vector<int32_t> windows(all_windows.begin() + static_cast<size_t>(row0) * W,
                                  all_windows.begin() + static_cast<size_t>(row0 + rows) * W);
     std::vector<StepPlan> plans;
@@ -1490,11 +1533,23 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     const bool transformer = decoder_family(spec.family);
     if (transformer) plan(windows, rows, run_steps, &plans, &max_slots, &max_tokens);
     const int splits_cap = std::max(1, (max_slots + 31) / 32);
-    int st = ensure_workspace(rows, run_steps, max_slots, max_tokens, splits_cap, history);
+    int st = ensure_workspace(rows, run_steps, max_slots, max_tokens, splits_cap, hist_rows);
     if (st) return st;
+    hist_count = hist_rows;
 
     cudaError_t err = cudaMemcpyAsync(ws.window, windows.data(), sizeof(int32_t) * windows.size(),
                                       cudaMemcpyHostToDevice, stream);
+    if (!err && history) {
+        err = cudaMemcpyAsync(ws.hist_rows_of, hist_local.data(), sizeof(int) * hist_rows,
+                              cudaMemcpyHostToDevice, stream);
+    }
+    // Host-side fault injection for tests of the failure path: the status word starts out set,
+    // as a kernel that gave up on a bounded wait leaves it. No kernel is made to fail.
+    int injected = 0;
+    if (const char* inject = std::getenv("BST_INJECT_PIPELINE_ERROR")) injected = std::atoi(inject);
+    if (!err && injected) {
+        err = cudaMemcpyAsync(ws.err, &injected, sizeof(int), cudaMemcpyHostToDevice, stream);
+    }
     if (!err) err = cudaMemsetAsync(ws.step, 0, sizeof(int), stream);
     if (!err) err = cudaMemsetAsync(ws.done, 0, sizeof(int), stream);
     if (!err) err = cudaMemsetAsync(ws.err, 0, sizeof(int), stream);
@@ -1548,7 +1603,7 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
             std::snprintf(key, sizeof(key), "%d/%d/%d/%d/%08x/%d/%d/%llu", static_cast<int>(mode),
                           rows, run_steps, ws.slots,
                           [&] { uint32_t b; std::memcpy(&b, &temperature, 4); return b; }(),
-                          top_k, history ? 1 : 0, static_cast<unsigned long long>(ws.generation));
+                          top_k, hist_rows, static_cast<unsigned long long>(ws.generation));
             if (!graph || graph_key != key) {
                 if (graph) {
                     cudaGraphExecDestroy(graph);
@@ -1606,11 +1661,19 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
             }
         }
         if (sink && mode != Mode::kScores) {
+            // The step's tokens and the pipeline status together: a step whose kernels gave up
+            // on a wait produced no tokens, and the sink must not see them.
+            int step_error = 0;
             err = cudaMemcpy2DAsync(step_tokens.data(), sizeof(int32_t), ws.tokens_out + g,
                                     sizeof(int32_t) * run_steps, sizeof(int32_t), rows,
                                     cudaMemcpyDeviceToHost, stream);
+            if (!err) {
+                err = cudaMemcpyAsync(&step_error, ws.err, sizeof(int), cudaMemcpyDeviceToHost,
+                                      stream);
+            }
             if (!err) err = cudaStreamSynchronize(stream);
             if (err) return cuda_fail(err, "reading tokens");
+            if (step_error) return fail(BST_PANIC, pipeline_message(step_error));
             for (int r = 0; r < rows; ++r) {
                 if (sink(user, row0 + r, g, step_tokens[r]) != 0) {
                     return fail(BST_INVALID, "the token sink stopped the call at row " +
@@ -1625,13 +1688,7 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     err = cudaMemcpyAsync(&pipeline_error, ws.err, sizeof(int), cudaMemcpyDeviceToHost, stream);
     if (!err) err = cudaStreamSynchronize(stream);
     if (err) return cuda_fail(err, "reading the pipeline status");
-    if (pipeline_error) {
-        if (pipeline_error == 11) {
-            return fail(BST_PANIC, "a grid barrier of the fused decode step timed out");
-        }
-        return fail(BST_PANIC, "a tensor-core GEMM pipeline wait timed out (stage " +
-                                   std::to_string(pipeline_error) + ")");
-    }
+    if (pipeline_error) return fail(BST_PANIC, pipeline_message(pipeline_error));
     if (mode == Mode::kScores) {
         std::vector<float> logits(static_cast<size_t>(rows) * V);
         err = cudaMemcpyAsync(logits.data(), ws.logits, sizeof(float) * logits.size(),
@@ -1644,9 +1701,16 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
         err = cudaMemcpyAsync(dst, ws.tokens_out, sizeof(int32_t) * static_cast<size_t>(rows) * steps,
                               tokens_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
                               stream);
-        if (!err && history) {
+        if (!err && history && watch.empty()) {
             err = cudaMemcpyAsync(logits + static_cast<size_t>(row0) * steps * V, ws.history,
                                   sizeof(float) * static_cast<size_t>(rows) * steps * V,
+                                  cudaMemcpyDeviceToHost, stream);
+        }
+        for (int h = 0; !err && history && !watch.empty() && h < hist_rows; ++h) {
+            if (hist_out[h] < 0) continue;
+            const size_t n = static_cast<size_t>(steps) * V;
+            err = cudaMemcpyAsync(logits + static_cast<size_t>(hist_out[h]) * n,
+                                  ws.history + static_cast<size_t>(h) * n, sizeof(float) * n,
                                   cudaMemcpyDeviceToHost, stream);
         }
         if (!err) err = cudaStreamSynchronize(stream);
@@ -2015,6 +2079,57 @@ int32_t bst_sample_logits(bst_engine h, const int32_t* contexts, int32_t rows, i
         return set_error(e, e->run(Mode::kSample, contexts, rows, length, steps, temperature,
                                    top_k, tokens, false, nullptr, nullptr, nullptr, logits));
     })
+}
+
+// bst_generate_logits / bst_sample_logits keeping the logits of `watch_count` chosen rows only.
+static int32_t logits_rows_call(bst_engine h, Mode mode, const int32_t* contexts, int32_t rows,
+                                int32_t length, int32_t steps, float temperature, int32_t top_k,
+                                int32_t* tokens, int32_t watch_count, const int32_t* watch_rows,
+                                float* logits) {
+    auto e = find_engine(h);
+    if (!e) return unknown(h);
+    BST_GUARDED({
+        std::lock_guard<std::mutex> lock(e->mu);
+        if (!logits) return set_error(e, e->fail(BST_INVALID, "logits must not be null"));
+        if (watch_count < 1 || !watch_rows) {
+            return set_error(e, e->fail(BST_INVALID, "watch_rows must name at least one row"));
+        }
+        std::vector<int32_t> watch(watch_rows, watch_rows + watch_count);
+        for (size_t i = 0; i < watch.size(); ++i) {
+            if (watch[i] < 0 || watch[i] >= rows) {
+                return set_error(e, e->fail(BST_INVALID, "watched row " + std::to_string(watch[i]) +
+                                                             " is outside [0, " +
+                                                             std::to_string(rows) + ")"));
+            }
+            for (size_t j = 0; j < i; ++j) {
+                if (watch[j] == watch[i]) {
+                    return set_error(e, e->fail(BST_INVALID, "watched row " +
+                                                                 std::to_string(watch[i]) +
+                                                                 " is named twice"));
+                }
+            }
+        }
+        e->watch = std::move(watch);
+        const int st = e->run(mode, contexts, rows, length, steps, temperature, top_k, tokens,
+                              false, nullptr, nullptr, nullptr, logits);
+        e->watch.clear();
+        return set_error(e, st);
+    })
+}
+
+int32_t bst_generate_logits_rows(bst_engine h, const int32_t* contexts, int32_t rows,
+                                 int32_t length, int32_t steps, int32_t* tokens,
+                                 int32_t watch_count, const int32_t* watch_rows, float* logits) {
+    return logits_rows_call(h, Mode::kGreedy, contexts, rows, length, steps, 1.0f, 1, tokens,
+                            watch_count, watch_rows, logits);
+}
+
+int32_t bst_sample_logits_rows(bst_engine h, const int32_t* contexts, int32_t rows,
+                               int32_t length, int32_t steps, float temperature, int32_t top_k,
+                               int32_t* tokens, int32_t watch_count, const int32_t* watch_rows,
+                               float* logits) {
+    return logits_rows_call(h, Mode::kSample, contexts, rows, length, steps, temperature, top_k,
+                            tokens, watch_count, watch_rows, logits);
 }
 
 static int32_t device_call(bst_engine h, Mode mode, const int32_t* contexts, int32_t rows,

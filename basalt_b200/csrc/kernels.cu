@@ -1057,14 +1057,16 @@ __global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict_
 }
 
 __global__ void k_stash_logits(const float* __restrict__ logits, int V, int steps,
-                               const int* __restrict__ step, float* __restrict__ history) {
+                               const int* __restrict__ step, const int* __restrict__ rows_of,
+                               float* __restrict__ history) {
     pdl_trigger();
     pdl_wait();
-    const int r = blockIdx.y;
+    const int h = blockIdx.y;
+    const int r = rows_of ? rows_of[h] : h;
     const int g = *step;
     const int v = blockIdx.x * blockDim.x + threadIdx.x;
     if (v < V) {
-        history[(static_cast<size_t>(r) * steps + g) * V + v] = logits[static_cast<size_t>(r) * V + v];
+        history[(static_cast<size_t>(h) * steps + g) * V + v] = logits[static_cast<size_t>(r) * V + v];
     }
 }
 
@@ -1382,9 +1384,10 @@ cudaError_t configure_device_kernels() {
 }
 
 cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,
-                                const int* step, float* history) {
+                                const int* step, const int* rows_of, float* history) {
     if (rows <= 0) return cudaSuccess;
-    return launch_pdl(k_stash_logits, dim3((V + 255) / 256, rows), 256, 0, s, logits, V, steps, step, history);
+    return launch_pdl(k_stash_logits, dim3((V + 255) / 256, rows), 256, 0, s, logits, V, steps, step,
+                      rows_of, history);
 }
 
 cudaError_t configure_device_kernels_once(int device) {

@@ -194,9 +194,10 @@ int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out);
 size_t tc_part_bytes_max();
 size_t tc_part_bytes(int M, int N, int K, int w_bf16);
 
-// Copies this step's logits [rows, V] to history[r][*step][v] (history: [rows, steps, V]).
+// Copies this step's logits of `rows` rows to history[h][*step][v] (history: [rows, steps, V]);
+// history row h holds logits row rows_of[h] (h itself when rows_of is null).
 cudaError_t launch_stash_logits(cudaStream_t s, const float* logits, int rows, int V, int steps,
-                                const int* step, float* history);
+                                const int* step, const int* rows_of, float* history);
 
 // ---- whole decode step in one persistent kernel (decode_fused.cu) ----
 // One layer's weights and cache for the fused step; an array of these lives in device memory.

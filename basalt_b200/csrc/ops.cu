@@ -53,19 +53,30 @@ size_t split_part_bytes(int64_t m, int64_t k, int64_t n) {
 }
 }  // namespace
 
-size_t matmul_scratch_bytes(int64_t m, int64_t k, int64_t n) {
+// Scratch of a matmul without its split-K partials: the error word and the operand planes (or the
+// transposed B of the GEMV path). The split-K partials come on top, as much room as is left.
+size_t matmul_fixed_scratch_bytes(int64_t m, int64_t k, int64_t n) {
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
     if (tc_usable(static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), 0)) {
         return up(sizeof(int)) + 2 * up(static_cast<size_t>(m) * k * 4) +
-               2 * up(static_cast<size_t>(n) * k * 4) + up(split_part_bytes(m, k, n));
+               2 * up(static_cast<size_t>(n) * k * 4);
     }
     return up(sizeof(int)) + up(static_cast<size_t>(n) * k * 4);
 }
 
-// Runs C = A * B with `scratch` (matmul_scratch_bytes of room, 256-byte aligned) as the only
-// device memory beyond A, B and C. Synchronises the stream to report pipeline errors.
+size_t matmul_scratch_bytes(int64_t m, int64_t k, int64_t n) {
+    auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    const bool tc = tc_usable(static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), 0);
+    return matmul_fixed_scratch_bytes(m, k, n) + (tc ? up(split_part_bytes(m, k, n)) : 0);
+}
+
+// Runs C = A * B with `scratch` (scratch_bytes of room, at least matmul_fixed_scratch_bytes,
+// 256-byte aligned) as the only device memory beyond A, B and C. The K split is planned for the
+// room left after the operand planes (fewer splits, or none, when it is short). Synchronises the
+// stream to report pipeline errors.
 int32_t matmul_with_scratch(cudaStream_t s, const float* a, const float* b, float* c, int64_t m,
-                            int64_t k, int64_t n, void* scratch, std::string* error) {
+                            int64_t k, int64_t n, void* scratch, size_t scratch_bytes,
+                            std::string* error) {
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
     char* p = static_cast<char*>(scratch);
     int* err = reinterpret_cast<int*>(p);
@@ -86,7 +97,9 @@ int32_t matmul_with_scratch(cudaStream_t s, const float* a, const float* b, floa
         float* bl = reinterpret_cast<float*>(p);
         p += up(static_cast<size_t>(n) * k * 4);
         float* part = reinterpret_cast<float*>(p);
-        const size_t part_bytes = split_part_bytes(m, k, n);
+        const size_t used = static_cast<size_t>(p - static_cast<char*>(scratch));
+        const size_t part_bytes =
+            std::min(split_part_bytes(m, k, n), scratch_bytes > used ? scratch_bytes - used : 0);
         if (!e) {
             k_transpose_split<<<tgrid, tblock, 0, s>>>(b, K, N, nullptr, bh, bl);
             e = cudaGetLastError();
@@ -160,13 +173,14 @@ extern "C" int32_t bst_matmul(int32_t device, void* stream, const float* a, cons
         return BST_PANIC;
     }
     void* scratch = nullptr;
-    e = cudaMallocAsync(&scratch, matmul_scratch_bytes(m, k, n), s);
+    const size_t scratch_bytes = matmul_scratch_bytes(m, k, n);
+    e = cudaMallocAsync(&scratch, scratch_bytes, s);
     if (e) {
         cudaGetLastError();
         set_thread_error(std::string("matmul: cannot allocate scratch: ") + cudaGetErrorString(e));
         return BST_OOM;
     }
-    st = matmul_with_scratch(s, a, b, c, m, k, n, scratch, &error);
+    st = matmul_with_scratch(s, a, b, c, m, k, n, scratch, scratch_bytes, &error);
     cudaFreeAsync(scratch, s);
     cudaStreamSynchronize(s);
     if (st) set_thread_error(error);

@@ -14,7 +14,9 @@
 // fault or, where the GPU can reach host memory, silently use the wrong memory. So the first call
 // on each device (with that device current) looks up the array's device address with
 // cudaGetSymbolAddress, checks the result, and caches it; later calls reuse that address. Make the
-// first call on a device before any stream capture.
+// first call on a device before any stream capture. A device reset (cudaDeviceReset, or a reset of
+// the primary context) unloads the module and invalidates the cached address: after one, the
+// process must not call this entry point again on that device.
 //
 // All calls share the one array and it keeps whatever the last call left in it; the part that must
 // start at zero (the pipeline error word) is cleared by every call.
@@ -30,9 +32,10 @@
 #include "kernels.h"
 
 namespace bst {
-size_t matmul_scratch_bytes(int64_t m, int64_t k, int64_t n);
+size_t matmul_fixed_scratch_bytes(int64_t m, int64_t k, int64_t n);
 int32_t matmul_with_scratch(cudaStream_t s, const float* a, const float* b, float* c, int64_t m,
-                            int64_t k, int64_t n, void* scratch, std::string* error);
+                            int64_t k, int64_t n, void* scratch, size_t scratch_bytes,
+                            std::string* error);
 int32_t check_matmul_args(const float* a, const float* b, float* c, int64_t m, int64_t k,
                           int64_t n, std::string* error);
 }  // namespace bst
@@ -75,7 +78,9 @@ extern "C" int32_t bst_matmul_static(int32_t device, void* stream, const float* 
         set_thread_error("matmul_static: device " + std::to_string(device) + " is out of range");
         return BST_INVALID;
     }
-    const size_t need = matmul_scratch_bytes(m, k, n);
+    // The operand planes must fit; the split-K partials take what room is left (fewer K splits,
+    // or none, when it is short).
+    const size_t need = matmul_fixed_scratch_bytes(m, k, n);
     if (k > 0 && need > kStaticScratchBytes) {
         set_thread_error("matmul_static: " + std::to_string(m) + "x" + std::to_string(k) + "x" +
                          std::to_string(n) + " needs " + std::to_string(need) +
@@ -108,7 +113,7 @@ extern "C" int32_t bst_matmul_static(int32_t device, void* stream, const float* 
         set_thread_error(std::string("matmul_static: ") + cudaGetErrorString(e));
         return BST_PANIC;
     }
-    st = matmul_with_scratch(s, a, b, c, m, k, n, scratch, &error);
+    st = matmul_with_scratch(s, a, b, c, m, k, n, scratch, kStaticScratchBytes, &error);
     if (st) set_thread_error(error);
     return st;
 }

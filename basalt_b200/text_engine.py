@@ -405,6 +405,32 @@ class TextEngine:
                                                logits.ctypes.data_as(_lib._f32p)))
         return tokens, logits
 
+    def generateWithLogitsOf(self, contexts, steps: int, rows: Sequence[int]):
+        """generateWithLogits keeping only the logits of `rows`: (tokens [N, steps],
+        logits [len(rows), steps, V])."""
+        arr = self._prepare(contexts, steps)
+        watch = np.ascontiguousarray(np.asarray(rows, dtype=np.int32))
+        tokens = np.zeros((arr.shape[0], steps), dtype=np.int32)
+        logits = np.zeros((watch.size, steps, self.vocabulary()), dtype=np.float32)
+        self._call(self._lib.bst_generate_logits_rows(
+            self._h, arr.ctypes.data_as(_lib._i32p), arr.shape[0], arr.shape[1], steps,
+            tokens.ctypes.data_as(_lib._i32p), watch.size, watch.ctypes.data_as(_lib._i32p),
+            logits.ctypes.data_as(_lib._f32p)))
+        return tokens, logits
+
+    def sampleWithLogitsOf(self, contexts, steps: int, temperature: float, topK: int,
+                           rows: Sequence[int]):
+        """sampleWithLogits keeping only the logits of `rows`."""
+        arr = self._prepare(contexts, steps)
+        watch = np.ascontiguousarray(np.asarray(rows, dtype=np.int32))
+        tokens = np.zeros((arr.shape[0], steps), dtype=np.int32)
+        logits = np.zeros((watch.size, steps, self.vocabulary()), dtype=np.float32)
+        self._call(self._lib.bst_sample_logits_rows(
+            self._h, arr.ctypes.data_as(_lib._i32p), arr.shape[0], arr.shape[1], steps,
+            float(np.float32(temperature)), int(topK), tokens.ctypes.data_as(_lib._i32p),
+            watch.size, watch.ctypes.data_as(_lib._i32p), logits.ctypes.data_as(_lib._f32p)))
+        return tokens, logits
+
     # ---- device-buffer entry points (callers that keep contexts and tokens in HBM) ----
     def generate_device(self, contexts_ptr: int, rows: int, length: int, steps: int,
                         tokens_ptr: int):

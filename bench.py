@@ -5,10 +5,15 @@ One step = one TextEngine.generateBatch call over the workload: every row's wind
 (prefill) and then ``steps`` tokens are decoded greedily for every row. The default workload is
 the batch-256 decode of a V4096 / d512 / 6-layer / 8-head / FFN2048 / window-512 padded decoder
 (256-token prompts, 256 new tokens per row, fp32 weights and cache); with N GPUs each rank decodes
-its own 256 rows (batch-sharded, no collective on the data path: weak scaling).
+its own 256 rows (batch-sharded, no collective on the data path: weak scaling). The same line
+carries the 8192-sequence sampled workload split over the N ranks (strong scaling, key ``c5``).
 
 Prints one JSON line (rank 0). ``--impl reference`` times the CPU restatement of the reference
-(full-window recompute per step, as TextEngine does) on the host cores instead.
+(full-window recompute per step, as TextEngine does) on the host cores instead; that arm never
+loads the CUDA library.
+
+Ranks talk through a gloo process group only (start/stop barriers and the maximum of the ranks'
+device times); nothing on the data path crosses GPUs.
 """
 from __future__ import annotations
 
@@ -19,7 +24,6 @@ import os
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from pathlib import Path
 
@@ -30,6 +34,20 @@ sys.path.insert(0, str(ROOT))
 
 DEFAULT_WORKLOAD = "v4096-d512-l6-w512-b256-greedy"
 BATCH1_WORKLOAD = "v8192-d768-l12-w1024-b1-greedy-bf16w"
+SCALING_WORKLOAD = "v8192-d768-l12-w1024-n8192-sampled-bf16w"
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one decode step of the named
+# workload from one ncu capture of its launches at 258 cached keys per row (summarised in the
+# profiles directory): the kernels other than attention move a fixed amount per step (weights,
+# split-K partials, activations), the attention kernels a fixed amount per (row, cached key), so
+# the step's traffic at the call's mean cache length is fixed + per_row_key * rows * length.
+NCU_STEP_TRAFFIC = {
+    # Per 128-row lane and layer: QKV 6.84 MB, O 2.65, fix-ups 1.35 + 4.24 + 4.49, FFN1 8.94,
+    # FFN2 10.51 (39.02 MB); 12 lane-layers plus the head's 17.33 MB. Attention: 138.02 MB for
+    # 128 rows x 258 keys per layer, 4 179 B per (row, key, layer).
+    "v4096-d512-l6-w512-b256-greedy": {"fixed": 12 * 39.02e6 + 17.33e6,
+                                       "per_row_key": 6 * 138.02e6 / (128 * 258)},
+}
 
 
 def parse():
@@ -41,6 +59,7 @@ def parse():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true")
+    ap.add_argument("--no-scaling", action="store_true", help="skip the 8192-sequence workload")
     ap.add_argument("--rows", type=int, default=0, help="override the workload's rows per GPU")
     ap.add_argument("--new-tokens", type=int, default=0, help="override tokens decoded per row")
     return ap.parse_args()
@@ -59,6 +78,30 @@ def measured_peaks():
         p = json.loads(path.read_text())
         return p["hbm_gbs"], p["bf16_tflops"], "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+def workload_of(args):
+    from dataclasses import replace
+
+    from basalt_b200.configs import config
+
+    workload = config(args.workload)
+    if args.rows or args.new_tokens:
+        workload = replace(workload, rows=args.rows or workload.rows,
+                           steps=args.new_tokens or workload.steps)
+    return workload
+
+
+def config_line(workload, rows_per_rank, world):
+    """The ``config`` object both arms print (the reference arm times the same workload)."""
+    m = workload.model
+    return {"workload": workload.name,
+            "model": f"padded decoder V{m.vocabulary} d{m.dimension} L{m.layers} H{m.heads} "
+                     f"F{m.hidden} W{m.window}",
+            "global_batch": rows_per_rank * world, "seq_len": m.window,
+            "prompt": workload.prompt, "new_tokens": workload.steps,
+            "parallelism": f"batch-sharded x{world}", "weights": m.weight_dtype,
+            "kv_cache": m.kv_dtype, "l2": "inputs larger than L2 (KV cache > 1 GB per GPU)"}
 
 
 class ClockSampler:
@@ -115,45 +158,60 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(workload, weights_path, threads=None, budget_s=15.0):
-    """The reference's algorithm on the host cores: every step re-runs Module.forward over the
-    full [rows, window] batch (TextEngine.generateBatch, TextEngine.java:232-254) with gemm.rs
-    numerics, on a bounded sample of the workload's rows and steps."""
-    from basalt_b200 import left_pad, synthetic_prompts
+# ---------------------------------------------------------------------------------------------
+# CPU side: the oracle (the reference's algorithm restated in C++), never the CUDA library.
+# ---------------------------------------------------------------------------------------------
+def oracle_engine(workload, weights_path):
     from oracle import oracle as orc
 
-    if threads:
-        orc.set_threads(threads)
     m = workload.model
-    oracle = orc.OracleEngine(orc.FAMILY_PADDED_DECODER, m.vocabulary, m.window, m.dimension,
+    engine = orc.OracleEngine(orc.FAMILY_PADDED_DECODER, m.vocabulary, m.window, m.dimension,
                               m.layers, m.heads, m.hidden)
-    oracle.load(weights_path)
-    rows = min(4, workload.rows)
-    prompts = synthetic_prompts(workload.prompt_seed, rows, workload.prompt, m.vocabulary)
-    ctx = left_pad(prompts, m.window, m.vocabulary)
+    engine.load(weights_path)
+    return engine
+
+
+def cpu_sample(engine, workload, rows, steps):
+    """Times TextEngine.generateBatch's algorithm (TextEngine.java:232-254: every step re-runs
+    Module.forward over the full [rows, window] batch, gemm.rs numerics) on `rows` rows of the
+    workload for `steps` steps. Returns (tokens/s, seconds)."""
+    from oracle import oracle as orc
+
+    m = workload.model
+    prompts = orc.synthetic_prompts(workload.prompt_seed, rows, workload.prompt, m.vocabulary)
+    ctx = orc.left_pad(prompts, m.window, m.vocabulary)
     t0 = time.perf_counter()
-    oracle.generate_batch(ctx, 1)
-    one = time.perf_counter() - t0
-    steps = int(max(1, min(workload.steps, budget_s / max(one, 1e-3))))
-    t0 = time.perf_counter()
-    oracle.generate_batch(ctx, steps)
+    engine.generate_batch(ctx, steps)
     elapsed = time.perf_counter() - t0
-    line = {"value": rows * steps / elapsed, "unit": "tokens/s", "cores": orc.threads(),
-            "kind": "port",
+    return rows * steps / elapsed, elapsed
+
+
+def cpu_baseline(workload, weights_path, budget_s=15.0):
+    """The reference's algorithm on the host cores, on a bounded sample of the workload's rows and
+    steps (``value``), plus the same model decoded the way a KV-cached CPU engine would
+    (``cached``)."""
+    from oracle import oracle as orc
+
+    engine = oracle_engine(workload, weights_path)
+    m = workload.model
+    rows = min(4, workload.rows)
+    _, one = cpu_sample(engine, workload, rows, 1)
+    steps = int(max(1, min(workload.steps, budget_s / max(one, 1e-3))))
+    value, elapsed = cpu_sample(engine, workload, rows, steps)
+    line = {"value": value, "unit": "tokens/s", "cores": orc.threads(), "kind": "port",
             "sample": f"{rows} rows x {steps} greedy steps of {workload.name}, full-window "
                       f"recompute per step ({elapsed:.1f} s)"}
-    # The same model decoded the way a cached CPU engine would (one token per row per step over a
-    # per-row KV cache), one row per host thread; decode rate from two runs that differ only in
-    # the number of steps, so the token-by-token prefill cancels.
+    # One row per host thread over a per-row KV cache; decode rate from two runs that differ only
+    # in the number of steps, so the token-by-token prefill cancels.
     crows = max(1, min(orc.threads(), workload.rows))
-    cprompts = synthetic_prompts(workload.prompt_seed, crows, workload.prompt, m.vocabulary)
-    cctx = left_pad(cprompts, m.window, m.vocabulary)
+    cctx = orc.left_pad(orc.synthetic_prompts(workload.prompt_seed, crows, workload.prompt,
+                                              m.vocabulary), m.window, m.vocabulary)
     t0 = time.perf_counter()
-    oracle.generate_batch_cached(cctx, 1)
+    engine.generate_batch_cached(cctx, 1)
     base = time.perf_counter() - t0
     extra = int(max(1, min(workload.steps - 1, 64)))
     t0 = time.perf_counter()
-    oracle.generate_batch_cached(cctx, 1 + extra)
+    engine.generate_batch_cached(cctx, 1 + extra)
     longer = time.perf_counter() - t0
     line["cached"] = {"value": crows * extra / max(1e-9, longer - base), "unit": "tokens/s",
                       "sample": f"{crows} rows x {extra} greedy steps over a per-row KV cache "
@@ -161,49 +219,103 @@ def cpu_baseline(workload, weights_path, threads=None, budget_s=15.0):
     return line
 
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of a kernel class, from one
-# ncu capture of the named workload (the commands are kept with the profile summaries):
-# "gemm_step": mean over the 25 projection launches of one lane's decode step (at ~258 cached
-# keys); "gemm": mean over the four prefill projections of one layer (M = 65 536 tokens).
-NCU_TRAFFIC = {
-    ("v4096-d512-l6-w512-b256-greedy", "gemm_step"): 7.64e6,
-    ("v4096-d512-l6-w512-b256-greedy", "gemm"): 0.956e9,
-}
+def run_reference(args, rank, world):
+    """The reference arm: the reference's CPU algorithm (the oracle) on this box's host cores, on
+    the GPU arm's workload, metric and config. Each step is one measured sample of 4 rows decoded
+    for a few full-window-recompute steps; nothing is extrapolated. Rank 0 alone runs."""
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    workload = workload_of(args)
+    m = workload.model
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "w.bin"
+        orc.write_synthetic_weights(m, path, workload.weight_seed)
+        engine = oracle_engine(workload, path)
+    rows = min(4, workload.rows)
+    _, one = cpu_sample(engine, workload, rows, 1)
+    # Steps per sample so that warm-up plus timed samples take about 90 s of host time.
+    per_sample_s = 90.0 / max(1, args.steps + args.warmup)
+    steps = int(max(1, min(workload.steps, per_sample_s / max(one, 1e-3))))
+    values, seconds = [], []
+    for i in range(args.warmup + args.steps):
+        value, elapsed = cpu_sample(engine, workload, rows, steps)
+        if i >= args.warmup:
+            values.append(value)
+            seconds.append(elapsed)
+    value = float(np.median(values))
+    sample = (f"{rows} rows x {steps} greedy steps of {workload.name} per step, full-window "
+              f"recompute per decoded token (TextEngine.generateBatch), median of {args.steps} "
+              f"samples")
+    line = {
+        "impl": "reference", "metric": "decode tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * float(np.mean(seconds)),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: N(0,0.02) weights from java.util.Random(0), prompts from "
+                f"java.util.Random({workload.prompt_seed}).nextInt({m.vocabulary})",
+        "config": config_line(workload, workload.rows, world),
+        "extrapolated": False,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": orc.threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
 
 
-def profile_summary(engine, run):
-    """Per-kernel device time of one call of `run`, CUDA events around every launch."""
+# ---------------------------------------------------------------------------------------------
+# GPU side.
+# ---------------------------------------------------------------------------------------------
+_WEIGHTS = {}
+
+
+def weights_file(model, seed, tmpdir):
+    """One synthetic weight file per (architecture, dtype, seed) for the whole run."""
+    from basalt_b200 import write_synthetic_weights
+
+    key = (model.family, model.vocabulary, model.window, model.dimension, model.layers,
+           model.heads, model.hidden, model.weight_dtype, seed)
+    if key not in _WEIGHTS:
+        path = Path(tmpdir) / f"w{len(_WEIGHTS)}.bin"
+        write_synthetic_weights(model, path, seed)
+        _WEIGHTS[key] = path
+    return _WEIGHTS[key]
+
+
+def open_engine(local, model, seed, tmpdir):
+    from basalt_b200 import Basalt, TextEngine
+
+    engine = TextEngine.of(Basalt.create(local), model, model.vocabulary, model.window)
+    engine.load(weights_file(model, seed, tmpdir))
+    return engine
+
+
+def event_time(stream, fn, reps):
+    """Median of `reps` separately timed calls of fn (CUDA events on the engine's stream)."""
     import torch
 
-    engine.profile(True)
-    engine.profile_reset()
-    run()
-    torch.cuda.synchronize()
-    prof = engine.profile_read()
-    engine.profile(False)
-    total_ms = sum(v["ms"] for v in prof.values()) or 1.0
-    kernels = {n: {"launches": v["launches"], "ms": round(v["ms"], 3),
-                   "share": round(v["ms"] / total_ms, 4),
-                   "GB/s": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1) if v["ms"] else None,
-                   "TFLOP/s": round(v["flops"] / (v["ms"] / 1000.0) / 1e12, 2) if v["ms"] else None}
-               for n, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
-    return prof, kernels
+    times = []
+    for _ in range(max(1, reps)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return float(np.median(times))
 
 
-def batch1(local, steps, warmup):
+def batch1(local, steps, warmup, tmpdir):
     """Single-stream latency: batch 1, 512-token prompt, 512 greedy tokens (bf16 weights)."""
     import torch
 
-    from basalt_b200 import (Basalt, TextEngine, config, left_pad, synthetic_prompts,
-                             write_synthetic_weights)
+    from basalt_b200 import config, left_pad, synthetic_prompts
 
     w = config(BATCH1_WORKLOAD)
     m = w.model
-    with tempfile.TemporaryDirectory() as tmp:
-        path = Path(tmp) / "w.bin"
-        write_synthetic_weights(m, path, w.weight_seed)
-        engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
-        engine.load(path)
+    engine = open_engine(local, m, w.weight_seed, tmpdir)
     ctx = left_pad(synthetic_prompts(w.prompt_seed, 1, w.prompt, m.vocabulary), m.window,
                    m.vocabulary)
     stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
@@ -218,79 +330,52 @@ def batch1(local, steps, warmup):
         call(w.steps, d_tok)
         call(1, d_one)
     torch.cuda.synchronize()
-
-    def timed(n, out, reps):
-        # Median of separately timed calls: the per-token figure is a difference of two call
-        # times, so one slow call would otherwise move it a lot.
-        times = []
-        for _ in range(max(3, reps)):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            call(n, out)
-            b.record(stream)
-            b.synchronize()
-            times.append(a.elapsed_time(b))
-        return float(np.median(times))
-
-    full_ms = timed(w.steps, d_tok, steps)
-    prefill_ms = timed(1, d_one, steps)
+    # The per-token figure is a difference of two call times: medians of separate calls.
+    full_ms = event_time(stream, lambda: call(w.steps, d_tok), max(3, steps))
+    prefill_ms = event_time(stream, lambda: call(1, d_one), max(3, steps))
     per_token_ms = (full_ms - prefill_ms) / (w.steps - 1)
-    prof, kernels = profile_summary(engine, lambda: call(w.steps, d_tok))
     hbm, _, src = measured_peaks()
-
-    def gbs(entry):
-        return entry["bytes"] / (entry["ms"] / 1000.0) / 1e9 if entry and entry["ms"] else None
-
-    step_gbs = gbs(prof.get("decode_step"))
-    # The same decode on the kernel-per-operation path (the fused step switched off), for the
-    # GEMV and attention kernels' own bandwidth.
+    # Algorithmic bytes of one decode step: every weight once, the cache each row reads (mean
+    # length over the call) and the logits row.
+    wb = 2 if m.weight_dtype == "bf16" else 4
+    kvb = 2 if m.kv_dtype == "bf16" else 4
+    params = m.layers * (4 * m.dimension ** 2 + 2 * m.dimension * m.hidden) + \
+        m.vocabulary * m.dimension
+    mean_len = w.prompt + (w.steps + 1) / 2.0
+    step_bytes = params * wb + m.layers * 2 * m.dimension * kvb * mean_len + m.vocabulary * 4
+    achieved = step_bytes / (per_token_ms / 1000.0) / 1e9
+    # The same decode on the kernel-per-operation path (the fused step switched off).
     os.environ["BST_FUSED_DECODE"] = "0"
     try:
-        unfused_ms = timed(w.steps, d_tok, max(1, steps // 2))
-        uprof, ukernels = profile_summary(engine, lambda: call(w.steps, d_tok))
+        call(w.steps, d_tok)
+        unfused_ms = event_time(stream, lambda: call(w.steps, d_tok), max(1, steps // 2))
     finally:
         del os.environ["BST_FUSED_DECODE"]
-    gemv_gbs = gbs(uprof.get("gemv"))
-    attn_gbs = gbs(uprof.get("attn_decode"))
     engine.close()
     return {"workload": w.name, "tokens_per_s": w.steps / (full_ms / 1000.0),
             "ms_per_call": full_ms, "prefill_ms": prefill_ms,
             "decode_ms_per_token": per_token_ms,
-            "decode_step_GBps": step_gbs, "decode_step_frac": step_gbs / hbm if step_gbs else None,
-            "kernels": kernels,
-            "per_operation_path": {
-                "decode_ms_per_token": (unfused_ms - prefill_ms) / (w.steps - 1),
-                "gemv_GBps": gemv_gbs, "gemv_frac": gemv_gbs / hbm if gemv_gbs else None,
-                "attn_decode_GBps": attn_gbs,
-                "attn_decode_frac": attn_gbs / hbm if attn_gbs else None,
-                "kernels": ukernels},
-            "peak_source": src}
+            "decode_step": {"kernel": "k_decode_step (one cooperative launch per token)",
+                            "bytes_per_step": step_bytes, "achieved": achieved,
+                            "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                            "peak_source": src},
+            "per_operation_path": {"decode_ms_per_token": (unfused_ms - prefill_ms) /
+                                   (w.steps - 1)}}
 
 
-def other_configs(local, reps=3):
+def other_configs(local, tmpdir, reps=3):
     """The other workloads of the scope table, timed on the device: C1 and C2 as per-call latency
     (L2-resident models), C3 with bf16 weights as decode tokens/s."""
     import torch
 
-    from basalt_b200 import (Basalt, TextEngine, config, left_pad, synthetic_prompts,
-                             write_synthetic_weights)
-
-    from dataclasses import replace
+    from basalt_b200 import config, left_pad, synthetic_prompts
 
     out = {}
     for name in ("v96-d128-l2-w64-b1-greedy", "v96-d256-l4-w128-b32-greedy",
-                 "v96-d256-l4-w128-b32-sampled", "v4096-d512-l6-w512-b256-greedy-bf16w",
-                 "v8192-d768-l12-w1024-n8192-sampled-bf16w"):
+                 "v96-d256-l4-w128-b32-sampled", "v4096-d512-l6-w512-b256-greedy-bf16w"):
         w = config(name)
-        if w.rows > 4096:
-            # 8192 sequences in waves of max_rows: 64 of the 512 tokens per row keep the call short
-            w = replace(w, steps=64)
         m = w.model
-        with tempfile.TemporaryDirectory() as tmp:
-            path = Path(tmp) / "w.bin"
-            write_synthetic_weights(m, path, w.weight_seed)
-            engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
-            engine.load(path)
+        engine = open_engine(local, m, w.weight_seed, tmpdir)
         ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
                        m.vocabulary)
         stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
@@ -306,24 +391,11 @@ def other_configs(local, reps=3):
             else:
                 engine.generate_device(d_ctx.data_ptr(), w.rows, ctx.shape[1], n, dst.data_ptr())
 
-        def timed(n, dst):
-            # Median of separately timed calls: the decode figure is a difference of two call
-            # times, so one slow call would otherwise move it a lot.
-            times = []
-            for _ in range(reps):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                call(n, dst)
-                b.record(stream)
-                b.synchronize()
-                times.append(a.elapsed_time(b))
-            return float(np.median(times))
-
         call(w.steps, d_tok)
         call(1, d_one)
         torch.cuda.synchronize()
-        full_ms = timed(w.steps, d_tok)
-        first_ms = timed(1, d_one)
+        full_ms = event_time(stream, lambda: call(w.steps, d_tok), reps)
+        first_ms = event_time(stream, lambda: call(1, d_one), reps)
         decode_ms = (full_ms - first_ms) / max(1, w.steps - 1)
         out[name] = {"rows": w.rows, "new_tokens": w.steps, "ms_per_call": full_ms,
                      "prefill_ms": first_ms, "decode_ms_per_step": decode_ms,
@@ -333,35 +405,43 @@ def other_configs(local, reps=3):
     return out
 
 
-def run_reference(args, rank, world):
-    from basalt_b200 import config, write_synthetic_weights
+def scaling_workload(local, rank, world, barrier, max_over_ranks, tmpdir):
+    """The 8192-sequence streamSampled workload (T = 1.0, seed 9, 128-token prompts, 512 tokens,
+    bf16 weights) split into contiguous row blocks over the ranks (strong scaling). Each rank's
+    generator starts where one engine seeded once would be at its first row, so the ranks together
+    draw exactly the unsharded run's tokens. One timed call per rank after a short warm-up call."""
+    import torch
 
-    if rank != 0:
-        return
-    workload = config(args.workload)
-    with tempfile.TemporaryDirectory() as tmp:
-        path = Path(tmp) / "w.bin"
-        write_synthetic_weights(workload.model, path, workload.weight_seed)
-        values = []
-        base = None
-        for i in range(args.warmup + args.steps):
-            base = cpu_baseline(workload, path, budget_s=max(2.0, 60.0 / (args.steps + args.warmup)))
-            if i >= args.warmup:
-                values.append(base["value"])
-    value = float(np.median(values))
-    line = {
-        "impl": "reference", "metric": "decode tokens/s", "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * workload.rows * workload.steps / value,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": workload.name, "global_batch": workload.rows * args.gpus,
-                   "seq_len": workload.model.window},
-        "cpu_baseline": {**base, "value": value},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    from basalt_b200 import config, left_pad, synthetic_prompts
+    from basalt_b200.sharding import shard_rng_state, shard_rows
+
+    w = config(SCALING_WORKLOAD)
+    m = w.model
+    first, R = shard_rows(w.rows, world, rank)
+    engine = open_engine(local, m, w.weight_seed, tmpdir)
+    prompts = synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary)
+    ctx = left_pad(prompts[first:first + R], m.window, m.vocabulary)
+    stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
+    d_ctx = torch.from_numpy(ctx).to(f"cuda:{local}")
+    d_tok = torch.empty((R, w.steps), dtype=torch.int32, device=f"cuda:{local}")
+
+    def call(steps):
+        engine.rng_state = shard_rng_state(w.sample_seed, steps, first)
+        engine.sample_device(d_ctx.data_ptr(), R, ctx.shape[1], steps, w.temperature, w.k,
+                             d_tok.data_ptr())
+
+    call(8)
+    torch.cuda.synchronize()
+    barrier()
+    ms = event_time(stream, lambda: call(w.steps), 1)
+    barrier()
+    per_rank = max_over_ranks(ms, gather=True)
+    engine.close()
+    slowest = max(per_rank)
+    return {"workload": w.name, "sequences": w.rows, "rows_per_rank": R, "new_tokens": w.steps,
+            "scaling": "strong", "n_gpus": world, "ms": slowest,
+            "tokens_per_s": w.rows * w.steps / (slowest / 1000.0),
+            "per_rank_ms": per_rank, "spread": slowest / min(per_rank)}
 
 
 def main():
@@ -373,8 +453,7 @@ def main():
 
     import torch
 
-    from basalt_b200 import (Basalt, TextEngine, config, left_pad, synthetic_prompts,
-                             write_synthetic_weights)
+    from basalt_b200 import _lib, left_pad, synthetic_prompts
 
     torch.cuda.set_device(local)
     dist = None
@@ -383,34 +462,38 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
 
-    workload = config(args.workload)
-    if args.rows or args.new_tokens:
-        from dataclasses import replace
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
 
-        workload = replace(workload, rows=args.rows or workload.rows,
-                           steps=args.new_tokens or workload.steps)
-    m = workload.model
+    def max_over_ranks(value, gather=False):
+        if not dist:
+            return [value] if gather else value
+        if gather:
+            out = [None] * world
+            dist.all_gather_object(out, value)
+            return out
+        t = torch.tensor([value], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     tmp = tempfile.TemporaryDirectory()
-    wpath = Path(tmp.name) / "w.bin"
-    write_synthetic_weights(m, wpath, workload.weight_seed)
-    engine = TextEngine.of(Basalt.create(local), m, m.vocabulary, m.window)
-    engine.load(wpath)
+    workload = workload_of(args)
+    m = workload.model
+    engine = open_engine(local, m, workload.weight_seed, tmp.name)
 
     # This rank's contiguous shard of one seeded draw of rows x world prompts (weak scaling:
-    # `rows` per GPU). Sampling workloads start the shard's generator where the unsharded run
-    # would be at its first row.
-    from basalt_b200.sharding import shard_rng_state, shard_rows
+    # `rows` per GPU).
+    from basalt_b200.sharding import shard_rows
 
     first, R = shard_rows(workload.rows * world, world, rank)
     prompts = synthetic_prompts(workload.prompt_seed, workload.rows * world, workload.prompt,
                                 m.vocabulary)
     ctx = left_pad(prompts[first:first + R], m.window, m.vocabulary)
     steps = workload.steps
-    if workload.mode == "sample":
-        engine.rng_state = shard_rng_state(workload.sample_seed, steps, first)
 
     stream = torch.cuda.ExternalStream(engine.cuda_stream(), device=torch.device("cuda", local))
     d_ctx = torch.from_numpy(ctx).to(f"cuda:{local}")
@@ -422,17 +505,11 @@ def main():
 
     for _ in range(args.warmup):
         device_step()
-    torch.cuda.synchronize()
-
-    def barrier():
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
+    barrier()
 
     launches0 = engine.stats()["launches"]
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
-    barrier()
     with ClockSampler(local) as clocks:
         start.record(stream)
         for _ in range(args.steps):
@@ -441,19 +518,13 @@ def main():
         stop.synchronize()
     barrier()
     launches = engine.stats()["launches"] - launches0
-    ms = start.elapsed_time(stop)
-    if dist:
-        t = torch.tensor([ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(start.elapsed_time(stop))
     tokens_per_step = R * steps * world
     value = tokens_per_step * args.steps / (ms / 1000.0)
 
     # End to end through the C ABI with host buffers: pinned contexts in, tokens out, every step.
     h_ctx = torch.from_numpy(ctx).pin_memory()
     h_tok = torch.empty((R, steps), dtype=torch.int32).pin_memory()
-    from basalt_b200 import _lib
-
     lib = _lib.load()
 
     def host_step():
@@ -473,106 +544,83 @@ def main():
     e2e_stop.record(stream)
     e2e_stop.synchronize()
     barrier()
-    e2e_ms = e2e_start.elapsed_time(e2e_stop)
-    if dist:
-        t = torch.tensor([e2e_ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_stop))
     e2e_value = tokens_per_step * args.steps / (e2e_ms / 1000.0)
 
-    # Prefill alone (one decoded token) vs the whole call: decode-only throughput.
+    # Prefill alone (one decoded token) against the whole call: the decode steps' share.
     d_one = torch.empty((R, 1), dtype=torch.int32, device=f"cuda:{local}")
     engine.generate_device(d_ctx.data_ptr(), R, ctx.shape[1], 1, d_one.data_ptr())
     torch.cuda.synchronize()
-    one_ms = []
-    for _ in range(3):  # median of separately timed calls
-        one_start = torch.cuda.Event(enable_timing=True)
-        one_stop = torch.cuda.Event(enable_timing=True)
-        one_start.record(stream)
-        engine.generate_device(d_ctx.data_ptr(), R, ctx.shape[1], 1, d_one.data_ptr())
-        one_stop.record(stream)
-        one_stop.synchronize()
-        one_ms.append(one_start.elapsed_time(one_stop))
-    prefill_ms = float(np.median(one_ms))
+    prefill_ms = event_time(
+        stream, lambda: engine.generate_device(d_ctx.data_ptr(), R, ctx.shape[1], 1,
+                                               d_one.data_ptr()), 3)
     step_ms = ms / args.steps
-    decode_tps = R * (steps - 1) / max(1e-9, (step_ms - prefill_ms) / 1000.0)
+    decode_ms = (step_ms - prefill_ms) / max(1, steps - 1)
+    decode_tps = R / max(1e-12, decode_ms / 1000.0)
 
-    # The decode step as a whole against HBM: every weight once plus the K/V every row reads
-    # (mean cache length over the call), per decode step.
+    # Roofline of the decode step, timed by CUDA events on the engine's stream over the timed
+    # calls: one step is one CUDA graph (every layer's projections, attention, fix-ups and the
+    # selection) replayed per token. Algorithmic bytes: every weight once plus the K/V each row
+    # reads at the call's mean cache length.
+    hbm_peak, bf16_peak, peak_src = measured_peaks()
     kvb = 2 if m.kv_dtype == "bf16" else 4
     wbytes = 2 if m.weight_dtype == "bf16" else 4
-    params = m.layers * (4 * m.dimension ** 2 + 2 * m.dimension * m.hidden) + m.vocabulary * m.dimension
+    params = m.layers * (4 * m.dimension ** 2 + 2 * m.dimension * m.hidden) + \
+        m.vocabulary * m.dimension
     mean_len = min(m.window, workload.prompt + (steps + 1) / 2.0)
-    step_bytes = R * m.layers * 2 * m.dimension * kvb * mean_len + params * wbytes
-    step_s = max(1e-12, (step_ms - prefill_ms) / 1000.0 / max(1, steps - 1))
-    hbm_peak, _, _ = measured_peaks()
-    step_hbm = {"achieved": step_bytes / step_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                "frac": step_bytes / step_s / 1e9 / hbm_peak, "bytes_per_step": step_bytes,
-                "mean_cache_len": mean_len}
-
-    # Per-kernel device time with CUDA events around each launch (one instrumented step).
-    prof, kernels = profile_summary(engine, device_step)
-    top = max(prof.items(), key=lambda kv: kv[1]["ms"])
-    name, k = top
-    hbm, bf16, peak_src = measured_peaks()
-
-    def tensor_roofline(cls, k):
-        per_launch_s = k["ms"] / 1000.0 / k["launches"]
-        achieved = k["flops"] / k["launches"] / per_launch_s / 1e12
-        # fp32 weights run as 3xTF32 (three tf32 passes, tf32 at half the bf16 rate); bf16
-        # weights as two bf16 passes: the ceiling for useful flops is the bf16 peak over that.
-        passes, rate = (2, 1.0) if m.weight_dtype == "bf16" else (3, 0.5)
-        useful_peak = bf16 * rate / passes
-        return {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                "frac": achieved / bf16, "traffic": None, "kernel": cls, "peak_source": peak_src,
-                "tensor_passes": passes, "useful_flops_peak": useful_peak,
-                "useful_frac": achieved / useful_peak}
-
-    def hbm_roofline(cls, k):
-        per_launch_s = k["ms"] / 1000.0 / k["launches"]
-        achieved = k["bytes"] / k["launches"] / per_launch_s / 1e9
-        return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": None, "kernel": cls, "peak_source": peak_src}
-
-    # Prefill GEMMs ("gemm", M = prompt tokens) are tensor-bound; the decode step's GEMMs
-    # ("gemm_step", M = 128 rows per lane) stream their weights once per step: HBM / latency.
-    roofline = tensor_roofline(name, k) if name == "gemm" else hbm_roofline(name, k)
-    roofline["traffic"] = NCU_TRAFFIC.get((workload.name, name))
+    kv_bytes = R * m.layers * 2 * m.dimension * kvb * mean_len
+    step_bytes = kv_bytes + params * wbytes
+    achieved = step_bytes / max(1e-12, decode_ms / 1000.0) / 1e9
+    traffic = NCU_STEP_TRAFFIC.get(workload.name)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak,
+                "traffic": (traffic["fixed"] + traffic["per_row_key"] * R * mean_len)
+                if traffic and R == 256 else None,
+                "kernel": "decode step (CUDA graph of the step's kernels)",
+                "algorithmic_bytes": step_bytes, "ms": decode_ms, "peak_source": peak_src}
+    # Prefill: the projections' useful flops (2 M N K over every layer and the head's last rows)
+    # against the tensor peak; fp32 weights run as 3xTF32 (three tf32 passes at half the bf16
+    # rate), bf16 weights as two bf16 passes.
+    tokens = R * workload.prompt
+    d, F = m.dimension, m.hidden
+    prefill_flops = 2.0 * tokens * m.layers * (4 * d * d + 2 * d * F) + 2.0 * R * d * m.vocabulary
+    passes, rate = (2, 1.0) if m.weight_dtype == "bf16" else (3, 0.5)
+    prefill_tflops = prefill_flops / (prefill_ms / 1000.0) / 1e12
+    prefill_roof = {"bound": "tensor", "achieved": prefill_tflops, "peak": bf16_peak,
+                    "unit": "TFLOP/s", "frac": prefill_tflops / bf16_peak,
+                    "tensor_passes": passes, "useful_flops_peak": bf16_peak * rate / passes,
+                    "useful_frac": prefill_tflops / (bf16_peak * rate / passes),
+                    "note": "whole prefill call (projections, attention, LayerNorms) against "
+                            "the projections' flops", "peak_source": peak_src}
 
     line = {
         "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16" if m.weight_dtype == "bf16" else "f32",
         "data": "synthetic: N(0,0.02) weights from java.util.Random(0), prompts from "
                 f"java.util.Random({workload.prompt_seed}).nextInt({m.vocabulary})",
-        "config": {"workload": workload.name, "model": f"padded decoder V{m.vocabulary} "
-                   f"d{m.dimension} L{m.layers} H{m.heads} F{m.hidden} W{m.window}",
-                   "global_batch": R * world, "seq_len": m.window, "prompt": workload.prompt,
-                   "new_tokens": steps, "parallelism": f"batch-sharded x{world}",
-                   "weights": m.weight_dtype, "kv_cache": m.kv_dtype,
-                   "l2": "inputs larger than L2 (KV cache > 1 GB per GPU)"},
+        "config": config_line(workload, R, world),
         "prefill_ms": prefill_ms, "decode_tokens_per_s": decode_tps * world,
-        "decode_step_hbm": step_hbm,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(ctx.nbytes), "d2h_bytes_per_step": int(R * steps * 4)},
         "gpu_launches": int(launches),
         "roofline": roofline,
-        "roofline_prefill_gemm": (
-            {**tensor_roofline("gemm", prof["gemm"]),
-             "traffic": NCU_TRAFFIC.get((workload.name, "gemm"))} if "gemm" in prof else None),
-        "kernels": kernels,
+        "roofline_prefill": prefill_roof,
         "clocks": clocks.summary(),
     }
+    engine.close()
+    if not args.no_scaling:
+        line["c5"] = scaling_workload(local, rank, world, barrier, max_over_ranks, tmp.name)
     if rank == 0 and world == 1 and not args.no_batch1:
-        line["batch1"] = batch1(local, max(1, args.steps), max(1, args.warmup))
-        line["configs"] = other_configs(local)
+        line["batch1"] = batch1(local, max(1, args.steps), max(1, args.warmup), tmp.name)
+        line["configs"] = other_configs(local, tmp.name)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(workload, wpath)
+        line["cpu_baseline"] = cpu_baseline(workload, weights_file(m, workload.weight_seed,
+                                                                   tmp.name))
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-    engine.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
 

@@ -6,8 +6,8 @@
  * through JNI (src/main/java/basalt/nativebridge/NativeBindings.java:13-89, implemented by
  * native/src/api.rs:118-709). This library replaces that per-op traffic with one call per
  * TextEngine method: the whole decode loop — embedding, LayerNorm, projections, attention over an
- * HBM KV cache, LM head, argmax or seeded sampling — runs on the GPU. A JNI shim (see
- * INTEGRATION.md) maps each TextEngine method onto the entry point named in its comment.
+ * HBM KV cache, LM head, argmax or seeded sampling — runs on the GPU. A JNI shim maps each
+ * TextEngine method onto the entry point named in its comment.
  *
  * Conventions (native/src/error.rs:9-17, src/main/java/basalt/BasaltExceptionCode.java:7-15):
  * every entry returns 0 on success or a negative status; the message of the last failure is
@@ -120,6 +120,18 @@ int32_t bst_generate_logits(bst_engine engine, const int32_t* contexts, int32_t 
 int32_t bst_sample_logits(bst_engine engine, const int32_t* contexts, int32_t rows,
                           int32_t length, int32_t steps, float temperature, int32_t top_k,
                           int32_t* tokens, float* logits);
+
+/* bst_generate_logits / bst_sample_logits that keep the logits of `watch_count` chosen rows only:
+ * logits [watch_count, steps, vocabulary], entry i for row watch_rows[i]. Lets a caller follow a
+ * few sequences of a batch too large for every row's logits (TextEngine.scores of those rows'
+ * windows at each step). Rows must be distinct and inside [0, rows). */
+int32_t bst_generate_logits_rows(bst_engine engine, const int32_t* contexts, int32_t rows,
+                                 int32_t length, int32_t steps, int32_t* tokens,
+                                 int32_t watch_count, const int32_t* watch_rows, float* logits);
+int32_t bst_sample_logits_rows(bst_engine engine, const int32_t* contexts, int32_t rows,
+                               int32_t length, int32_t steps, float temperature, int32_t top_k,
+                               int32_t* tokens, int32_t watch_count, const int32_t* watch_rows,
+                               float* logits);
 
 /* The same two calls for callers whose contexts and token buffers already live on the engine's
  * device (device pointers; no sink). */

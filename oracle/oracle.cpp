@@ -453,7 +453,10 @@ int embedding(orc_engine* e, const float* ids, int64_t rows, const std::vector<f
 // position embeddings, a final LayerNorm, the last-position slice (Tensor.slice,
 // torch/Tensor.java:321-338) and a Linear head. For the padded family the position of a token
 // counts from the first non-PAD id of its row, and the additive mask also hides PAD key columns.
-int decoder_forward(orc_engine* e, const float* ids, int64_t rows, float* logits) {
+// Logits are written for window positions first_out..W-1 of every row ([rows, W - first_out, V]);
+// TextEngine reads the last position only (first_out = W - 1).
+int decoder_forward(orc_engine* e, const float* ids, int64_t rows, float* logits,
+                    int64_t first_out) {
     const orc_spec& s = e->spec;
     const int64_t W = s.window, d = s.dimension, H = s.heads, hd = d / H, F = s.hidden;
     const int64_t V = s.vocabulary, T = rows * W;
@@ -548,11 +551,13 @@ int decoder_forward(orc_engine* e, const float* ids, int64_t rows, float* logits
     // Final LayerNorm, then slice(1, W-1, W) -> [rows, d], then the head.
     layer_norm(x.data(), e->p("norm.gamma").data(), e->p("norm.beta").data(), h.data(), T, d,
                kLayerNormEps);
-    std::vector<float> last(rows * d);
+    const int64_t outs = W - first_out;
+    std::vector<float> last(rows * outs * d);
     for (int64_t r = 0; r < rows; ++r) {
-        std::memcpy(last.data() + r * d, h.data() + (r * W + W - 1) * d, sizeof(float) * d);
+        std::memcpy(last.data() + r * outs * d, h.data() + (r * W + first_out) * d,
+                    sizeof(float) * outs * d);
     }
-    linear(e, last.data(), rows, d, V, "head", logits);
+    linear(e, last.data(), rows * outs, d, V, "head", logits);
     return 0;
 }
 
@@ -600,7 +605,7 @@ int last_token_forward(orc_engine* e, const float* ids, int64_t rows, float* log
 int forward(orc_engine* e, const float* ids, int64_t rows, float* logits) {
     switch (e->spec.family) {
         case ORC_FAMILY_PADDED_DECODER:
-        case ORC_FAMILY_DECODER: return decoder_forward(e, ids, rows, logits);
+        case ORC_FAMILY_DECODER: return decoder_forward(e, ids, rows, logits, e->spec.window - 1);
         case ORC_FAMILY_CHAR_LM: return char_lm_forward(e, ids, rows, logits);
         case ORC_FAMILY_LAST_TOKEN: return last_token_forward(e, ids, rows, logits);
         default: return e->fail(-8, "unknown model family");
@@ -1132,6 +1137,102 @@ extern "C" int32_t orc_forced_scores(orc_engine* e, const int32_t* context, int3
         push(carried[0], forced[step]);
     }
     return 0;
+}
+
+// Teacher-forced logits of the padded decoder from one causal pass per row. While a row's window
+// still starts with PAD at every step (steps - 1 <= leading PADs < W), the window scored at step g
+// holds exactly the row's real tokens followed by forced[0..g-1], at positions counted from the
+// first real token, and every PAD key is masked out (exp(-1e9 - max) is 0 in f32). The logits of
+// step g are then the logits at position (real prompt length - 1 + g) of one forward over the
+// real prompt followed by forced[0..steps-2]: the same sums TextEngine's full-window recompute
+// forms (TextEngine.java:96-112, MultiheadAttention.java:40-82), with the matrix products taken
+// at a different row count, so only the gemm.rs FMA-region membership of a row can differ.
+// Returns -8 when a row's window would drop a real token; orc_forced_scores covers that case.
+extern "C" int32_t orc_forced_scores_single_pass(orc_engine* e, const int32_t* contexts,
+                                                 int32_t rows, int32_t length, int32_t steps,
+                                                 const int32_t* forced, float* logits) {
+    if (e->spec.family != ORC_FAMILY_PADDED_DECODER) {
+        return e->fail(-8, "the single-pass teacher-forced logits restate the padded decoder");
+    }
+    int status = require_steps(e, steps);
+    if (status) return status;
+    if (rows < 1) return e->fail(-1, "contexts must not be empty");
+    status = require_context(e, length);
+    if (status) return status;
+    const int32_t W = e->spec.window, V = e->spec.vocabulary;
+    const float pad = static_cast<float>(V);
+    std::vector<float> ids(static_cast<size_t>(rows) * W);
+    for (int32_t r = 0; r < rows; ++r) {
+        const std::vector<int32_t> w = tail(e, contexts + int64_t(r) * length, length);
+        int32_t npad = 0;
+        while (npad < W && w[npad] == V) ++npad;
+        if (npad == W || steps - 1 > npad) {
+            return e->fail(-8, "row " + std::to_string(r) + ": the window drops a real token "
+                               "within the forced steps");
+        }
+        // Left-pad (prompt real tokens, forced[0..steps-2]) to the window.
+        float* row = ids.data() + int64_t(r) * W;
+        const int32_t lead = npad - (steps - 1);
+        for (int32_t t = 0; t < lead; ++t) row[t] = pad;
+        for (int32_t t = npad; t < W; ++t) row[lead + t - npad] = static_cast<float>(w[t]);
+        for (int32_t g = 0; g + 1 < steps; ++g) {
+            const int32_t id = forced[int64_t(r) * steps + g];
+            if (id < 0 || id >= V) return e->fail(-1, "forced token outside the vocabulary");
+            row[W - (steps - 1) + g] = static_cast<float>(id);
+        }
+    }
+    // Rows in groups of four bound the [rows, H, W, W] attention scores.
+    for (int32_t r0 = 0; r0 < rows; r0 += 4) {
+        const int32_t n = std::min<int32_t>(4, rows - r0);
+        status = decoder_forward(e, ids.data() + int64_t(r0) * W, n,
+                                 logits + int64_t(r0) * steps * V, W - steps);
+        if (status) return status;
+    }
+    return 0;
+}
+
+// Synthetic weights: every parameter N(0, stddev) from java.util.Random(seed).nextGaussian in
+// namedParameters order, LayerNorm gamma 1 and beta 0, matrices and embedding tables rounded to
+// bf16 (round to nearest even) when round_bf16 != 0. The LastTokenModel keeps its fixture weights.
+extern "C" int32_t orc_fill_synthetic(orc_engine* e, int64_t seed, double stddev,
+                                      int32_t round_bf16) {
+    if (e->spec.family == ORC_FAMILY_LAST_TOKEN) return 0;
+    orc_random random;
+    orc_random_set_seed(&random, seed);
+    auto ends = [](const std::string& n, const char* suffix) {
+        const size_t k = std::strlen(suffix);
+        return n.size() >= k && n.compare(n.size() - k, k, suffix) == 0;
+    };
+    for (size_t i = 0; i < e->names.size(); ++i) {
+        const std::string& n = e->names[i];
+        std::vector<float>& v = e->values[i];
+        if (n.find("norm") != std::string::npos && (ends(n, ".gamma") || ends(n, ".beta"))) {
+            std::fill(v.begin(), v.end(), ends(n, ".gamma") ? 1.0f : 0.0f);
+            continue;
+        }
+        const bool matrix = e->spec.family == ORC_FAMILY_CHAR_LM
+                                ? (n == "param0" || n == "param1" || n == "param3" || n == "param5")
+                                : ends(n, ".weight");
+        for (float& x : v) {
+            x = static_cast<float>(orc_random_next_gaussian(&random) * stddev);
+            if (round_bf16 && matrix && !std::isnan(x)) {
+                uint32_t u;
+                std::memcpy(&u, &x, 4);
+                u += 0x7fffu + ((u >> 16) & 1u);
+                u &= 0xffff0000u;
+                std::memcpy(&x, &u, 4);
+            }
+        }
+    }
+    return 0;
+}
+
+// Prompts of java.util.Random(seed).nextInt(bound) ids, row after row.
+extern "C" void orc_synthetic_prompts(int64_t seed, int32_t rows, int32_t length, int32_t bound,
+                                      int32_t* out) {
+    orc_random random;
+    orc_random_set_seed(&random, seed);
+    for (int64_t i = 0; i < int64_t(rows) * length; ++i) out[i] = orc_random_next_int_bound(&random, bound);
 }
 
 extern "C" int32_t orc_draw(orc_engine* e, const double* scores, int32_t count, float temperature,

@@ -117,6 +117,18 @@ void orc_set_rng_state(orc_engine* e, uint64_t state);
  * argmax, writing [steps, V] logits. Used to compare a GPU run step by step after a divergence. */
 int32_t orc_forced_scores(orc_engine* e, const int32_t* context, int32_t length, int32_t steps,
                           const int32_t* forced, float* logits);
+/* Teacher-forced logits of the padded decoder for `rows` rows ([rows, steps, V]), each row from
+ * one causal pass over its real prompt tokens and forced[r*steps .. r*steps+steps-2]. Valid while
+ * every step's window still starts with PAD (steps - 1 <= leading PADs < W); returns -8
+ * otherwise. Agrees with orc_forced_scores up to the rounding of the row count's FMA region. */
+int32_t orc_forced_scores_single_pass(orc_engine* e, const int32_t* contexts, int32_t rows,
+                                      int32_t length, int32_t steps, const int32_t* forced,
+                                      float* logits);
+/* Fills the parameters with N(0, stddev) from java.util.Random(seed).nextGaussian in parameter
+ * order (LayerNorm gamma 1, beta 0; matrices rounded to bf16 when round_bf16). */
+int32_t orc_fill_synthetic(orc_engine* e, int64_t seed, double stddev, int32_t round_bf16);
+/* java.util.Random(seed).nextInt(bound), rows * length values row after row. */
+void orc_synthetic_prompts(int64_t seed, int32_t rows, int32_t length, int32_t bound, int32_t* out);
 /* The reference's draw() on a given score row (TextEngine.java:403-427) with the engine RNG. */
 int32_t orc_draw(orc_engine* e, const double* scores, int32_t count, float temperature,
                  int32_t top_k);

@@ -109,6 +109,13 @@ def lib() -> ctypes.CDLL:
                                                    ctypes.c_int32, i32p, f32p]),
             "orc_draw": (ctypes.c_int32, [ctypes.c_void_p, f64p, ctypes.c_int32, ctypes.c_float,
                                           ctypes.c_int32]),
+            "orc_forced_scores_single_pass": (ctypes.c_int32, [ctypes.c_void_p, i32p,
+                                                               ctypes.c_int32, ctypes.c_int32,
+                                                               ctypes.c_int32, i32p, f32p]),
+            "orc_fill_synthetic": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64,
+                                                    ctypes.c_double, ctypes.c_int32]),
+            "orc_synthetic_prompts": (None, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                             ctypes.c_int32, i32p]),
             "orc_threads": (ctypes.c_int32, []),
             "orc_set_threads": (None, [ctypes.c_int32]),
         }
@@ -361,10 +368,64 @@ class OracleEngine:
                                             _ptr(out, ctypes.c_float)))
         return out
 
+    def forced_scores_rows(self, contexts, forced) -> np.ndarray:
+        """Teacher-forced logits [rows, steps, V] of several rows of the padded decoder.
+
+        ``forced[r]`` are the tokens row r pushes after each step. Rows whose window still starts
+        with PAD at every step take one causal pass each (``orc_forced_scores_single_pass``);
+        otherwise every step recomputes the full window, as TextEngine does."""
+        arr = self._contexts(contexts)
+        forced = np.ascontiguousarray(np.asarray(forced, dtype=np.int32).reshape(arr.shape[0], -1))
+        rows, steps = forced.shape
+        out = np.empty((rows, steps, self.vocabulary), dtype=np.float32)
+        status = lib().orc_forced_scores_single_pass(
+            self._h, _ptr(arr, ctypes.c_int32), rows, arr.shape[1], steps,
+            _ptr(forced, ctypes.c_int32), _ptr(out, ctypes.c_float))
+        if status == -8:
+            for r in range(rows):
+                out[r] = self.forced_scores(arr[r], forced[r])
+        else:
+            self._check(status)
+        return out
+
+    def fill_synthetic(self, seed: int, stddev: float = 0.02, round_bf16: bool = False):
+        """N(0, stddev) parameters from java.util.Random(seed).nextGaussian (LayerNorm 1 / 0)."""
+        self._check(lib().orc_fill_synthetic(self._h, seed, stddev, int(round_bf16)))
+
     def draw(self, scores, temperature: float, top_k: int) -> int:
         s = np.ascontiguousarray(scores, dtype=np.float64)
         return self._check(lib().orc_draw(self._h, _ptr(s, ctypes.c_double), s.size,
                                           temperature, top_k))
+
+
+def synthetic_prompts(seed: int, rows: int, length: int, bound: int) -> np.ndarray:
+    """[rows, length] ids of java.util.Random(seed).nextInt(bound), row after row."""
+    out = np.empty((rows, length), dtype=np.int32)
+    lib().orc_synthetic_prompts(seed, rows, length, bound, _ptr(out, ctypes.c_int32))
+    return out
+
+
+def left_pad(prompts: np.ndarray, window: int, pad: int) -> np.ndarray:
+    """Prompts left-padded with `pad` to at least `window` ids (TextEngine reads the tail)."""
+    prompts = np.asarray(prompts, dtype=np.int32)
+    if prompts.shape[1] >= window:
+        return np.ascontiguousarray(prompts[:, prompts.shape[1] - window:])
+    out = np.full((prompts.shape[0], window), pad, dtype=np.int32)
+    out[:, window - prompts.shape[1]:] = prompts
+    return out
+
+
+def write_synthetic_weights(model, path, seed: int, stddev: float = 0.02) -> "OracleEngine":
+    """Writes the TextEngine weight file of a synthetic model and returns the oracle bound to it.
+
+    ``model`` is any object with the ModelSpec fields (family name, sizes, weight_dtype)."""
+    family = {"padded_decoder": FAMILY_PADDED_DECODER, "decoder": FAMILY_DECODER,
+              "char_lm": FAMILY_CHAR_LM, "last_token": FAMILY_LAST_TOKEN}[model.family]
+    engine = OracleEngine(family, model.vocabulary, model.window, model.dimension, model.layers,
+                          model.heads, model.hidden)
+    engine.fill_synthetic(seed, stddev, model.weight_dtype == "bf16")
+    engine.save(path)
+    return engine
 
 
 def lcg_advance(state: int, steps: int) -> int:

@@ -69,32 +69,27 @@ def check_greedy_row(oracle, context, gpu_tokens, gpu_logits, report: Report, wh
 
 
 def draw_margin(scores: np.ndarray, temperature: float, top_k: int, state: int):
-    """Replays TextEngine.draw on `scores` with generator state `state`.
+    """Replays TextEngine.draw (TextEngine.java:403-427) on `scores` with generator state `state`.
 
-    Returns (token, relative distance of the target to the nearest cumulative boundary,
-    state after the draw)."""
-    scores = scores.astype(np.float64)
-    order = sorted(range(scores.size), key=lambda t: (-scores[t], t))
+    The stable descending sort is a lexicographic sort on (-score, index); ``total`` and the
+    running sum are sequential double sums in sorted order (np.cumsum adds left to right, as the
+    Java loop does). Returns (token, relative distance of the target to the nearest cumulative
+    boundary it passed, state after the draw)."""
+    scores = np.asarray(scores, dtype=np.float64)
+    order = np.lexsort((np.arange(scores.size), -scores))[:top_k]
     t = np.float64(np.float32(temperature))
-    w = np.exp((scores[order[:top_k]] - scores[order[0]]) / t)
-    total = 0.0
-    for x in w:
-        total += x
+    w = np.exp((scores[order] - scores[order[0]]) / t)
+    running = np.cumsum(w)
+    total = running[-1]
     state = orc.lcg_advance(state, 1)
     hi = state >> (48 - 26)
     state = orc.lcg_advance(state, 1)
     lo = state >> (48 - 27)
     target = float(((hi << 27) + lo) * 2.0 ** -53) * total
-    running = 0.0
-    chosen = order[top_k - 1]
-    margin = np.inf
-    for i, x in enumerate(w):
-        running += x
-        margin = min(margin, abs(target - running) / total)
-        if target <= running:
-            chosen = order[i]
-            break
-    return chosen, margin, state
+    i = int(np.searchsorted(running, target, side="left"))
+    i = min(i, top_k - 1)
+    margin = float(np.min(np.abs(target - running[:i + 1])) / total)
+    return int(order[i]), margin, state
 
 
 def check_sampled_row(oracle, context, gpu_tokens, gpu_logits, temperature, top_k, state,
@@ -111,3 +106,34 @@ def check_sampled_row(oracle, context, gpu_tokens, gpu_logits, temperature, top_
                 continue  # teacher forcing keeps both sides on the GPU's window
             report.mismatches.append((where, step, int(token), want))
     return state
+
+
+def check_rows(oracle, contexts, rows, gpu_tokens, gpu_logits, report: Report, where="",
+               atol=ATOL, rtol=RTOL, sampled=None):
+    """Teacher-forced comparison of several rows at once (oracle.forced_scores_rows).
+
+    gpu_tokens: [len(rows), steps]; gpu_logits: [len(rows), steps, V]. For sampled decoding pass
+    ``sampled=(temperature, top_k, states)`` with each row's generator state before its first
+    draw. Returns the oracle's logits and the per-step agreement of the GPU's tokens with the
+    oracle's choice."""
+    contexts = np.asarray(contexts)
+    ref = oracle.forced_scores_rows(contexts[list(rows)], gpu_tokens)
+    agree = []
+    for i, r in enumerate(rows):
+        here = f"{where} row {r}"
+        report.max_abs = max(report.max_abs,
+                             compare_logits(gpu_logits[i], ref[i], atol, rtol, here))
+        report.steps += gpu_tokens.shape[1]
+        state = sampled[2][i] if sampled else None
+        for step, token in enumerate(gpu_tokens[i]):
+            if sampled:
+                want, margin, state = draw_margin(ref[i, step], sampled[0], sampled[1], state)
+                near = margin < BOUNDARY_RTOL
+            else:
+                want = int(np.argmax(ref[i, step]))
+                near = top2_gap(ref[i, step]) < atol
+            agree.append(want == int(token))
+            if want != int(token):
+                (report.near_ties if near else report.mismatches).append(
+                    (here, step, int(token), want))
+    return ref, float(np.mean(agree)) if agree else 1.0

@@ -1,21 +1,44 @@
-"""Full-size workloads, checked through properties that do not need the oracle to replay every
-step: at sampled (row, step) points the decode-path token equals the argmax of the reference's
-full-window recompute of that step's window, the GPU's own full-window scores match the oracle's,
-and a row decoded inside the batch equals the row decoded alone up to a near tie."""
+"""Full-size workloads against the oracle, step by step under teacher forcing.
+
+Each test decodes a whole workload on the GPU and keeps the logits of rows spread over the batch
+(both decode lanes, several waves), then the oracle scores, for every step of those rows, the
+window the GPU scored (TextEngine.scores, TextEngine.java:96-112) and checks:
+
+* logits within |gpu - ref| <= 1e-3 + 1e-4 |ref| (fp32 arithmetic; bf16-stored weights that the
+  weight file holds exactly, so the oracle computes on the same values);
+* greedy tokens equal to the oracle's first-maximum argmax, sampled tokens equal to the oracle's
+  draw() from the row's java.util.Random state, except at reported near ties;
+* the tokens of the call that kept logits equal the tokens of the benchmarked call (no logits).
+
+A bf16 engine fed the fp32 weight file (conversion on load) is held to a stated looser logit
+tolerance and a token-agreement rate against the fp32 oracle. Every test prints one ``PARITY``
+line with its maximum |delta logit|, near ties and agreement rate.
+"""
+import json
+from dataclasses import replace
+
 import numpy as np
 import pytest
 
 from basalt_b200 import TextEngine, config, left_pad, synthetic_prompts, write_synthetic_weights
+from basalt_b200.sharding import shard_rng_state
 from oracle import oracle as orc
-from parity import ATOL, compare_logits, top2_gap
+from parity import Report, check_rows
 
 pytestmark = pytest.mark.gpu
 
+# bf16 weights converted on load from an fp32 file, against the fp32 oracle: bf16 rounding of every
+# matrix moves the logits by ~1e-2 at most on these N(0, 0.02) models (measured with the oracle
+# itself on bf16-rounded weights), and flips the argmax only where the top-2 gap is that small.
+BF16_ON_LOAD_ATOL = 5e-2
+BF16_ON_LOAD_MIN_AGREEMENT = 0.95
 
-def pair(runtime, workload, path):
+
+def pair(runtime, workload, path, engine_model=None):
     m = workload.model
     write_synthetic_weights(m, path, workload.weight_seed)
-    engine = TextEngine.of(runtime, m, m.vocabulary, m.window)
+    em = engine_model or m
+    engine = TextEngine.of(runtime, em, em.vocabulary, em.window)
     engine.load(path)
     oracle = orc.OracleEngine(orc.FAMILY_PADDED_DECODER, m.vocabulary, m.window, m.dimension,
                               m.layers, m.heads, m.hidden)
@@ -23,94 +46,108 @@ def pair(runtime, workload, path):
     return engine, oracle
 
 
-def window_at(ctx_row, tokens_row, step, window):
-    full = np.concatenate([ctx_row, tokens_row[:step]])
-    return full[-window:]
+def report_line(name, report, agreement, **extra):
+    line = {"test": name, "steps": report.steps, "max_abs_dlogit": report.max_abs,
+            "near_ties": len(report.near_ties), "mismatches": len(report.mismatches),
+            "token_agreement": agreement, **extra}
+    print("PARITY " + json.dumps(line))
 
 
-def check_points(engine, oracle, ctx, tokens, points, window):
-    for r, g in points:
-        win = window_at(ctx[r], tokens[r], g, window)
-        ref = oracle.scores(win)
-        compare_logits(engine.scores(win), ref, where=f"row {r} step {g}")
-        if int(np.argmax(ref)) != int(tokens[r, g]):
-            assert top2_gap(ref) < ATOL, f"row {r} step {g}: {tokens[r, g]} vs {np.argmax(ref)}"
+def assert_clean(report, rows):
+    assert not report.mismatches, f"token mismatches: {report.mismatches[:5]}"
+    assert len(report.near_ties) <= len(rows), report.near_ties
 
 
-def first_divergence_is_a_near_tie(oracle, ctx_row, a, b, window):
-    diff = np.nonzero(a != b)[0]
-    if diff.size == 0:
-        return True
-    g = int(diff[0])
-    return top2_gap(oracle.scores(window_at(ctx_row, a, g, window))) < ATOL
+def greedy_full(runtime, tmp_path, name, rows):
+    w = config(name)
+    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
+    m = w.model
+    ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
+                   m.vocabulary)
+    bench_tokens = engine.generateBatch(ctx, w.steps)
+    tokens, logits = engine.generateWithLogitsOf(ctx, w.steps, rows)
+    np.testing.assert_array_equal(tokens, bench_tokens)
+    report = Report()
+    _, agreement = check_rows(oracle, ctx, rows, tokens[rows], logits, report, name)
+    report_line(name, report, agreement, rows=list(rows))
+    assert_clean(report, rows)
+    return engine, ctx, tokens
 
 
-def test_v4096_d512_l6_batch256_greedy(runtime, tmp_path):
+def test_v4096_d512_l6_batch256_greedy_every_step(runtime, tmp_path):
+    # Rows from both decode lanes (0..127 and 128..255), all 256 steps.
+    greedy_full(runtime, tmp_path, "v4096-d512-l6-w512-b256-greedy",
+                [0, 63, 127, 128, 191, 255])
+
+
+def test_v4096_d512_l6_batch256_greedy_bf16_weights_every_step(runtime, tmp_path):
+    greedy_full(runtime, tmp_path, "v4096-d512-l6-w512-b256-greedy-bf16w", [0, 127, 128, 255])
+
+
+def test_v4096_d512_l6_bf16_conversion_on_load_agreement(runtime, tmp_path):
+    # The fp32 weight file into an engine that stores bf16 matrices (TextEngine.load keeps the
+    # file's fp32 values; the device store rounds them to bf16), against the fp32 oracle.
     w = config("v4096-d512-l6-w512-b256-greedy")
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
-    W, V = w.model.window, w.model.vocabulary
-    ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, V), W, V)
-    tokens = engine.generateBatch(ctx, w.steps)
-    assert tokens.shape == (256, 256) and tokens.min() >= 0 and tokens.max() < V
-    check_points(engine, oracle, ctx, tokens, [(0, 0), (0, 255), (131, 128), (255, 255)], W)
-    alone = engine.generate(ctx[77], w.steps)
-    assert first_divergence_is_a_near_tie(oracle, ctx[77], tokens[77], alone, W)
+    m = w.model
+    engine, oracle = pair(runtime, w, tmp_path / "w.bin", replace(m, weight_dtype="bf16"))
+    rows = [0, 100, 200, 255]
+    ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
+                   m.vocabulary)
+    tokens, logits = engine.generateWithLogitsOf(ctx, w.steps, rows)
+    report = Report()
+    _, agreement = check_rows(oracle, ctx, rows, tokens[rows], logits, report,
+                              "bf16-on-load", atol=BF16_ON_LOAD_ATOL, rtol=0.0)
+    report_line("v4096-d512-l6-bf16-on-load", report, agreement, rows=rows,
+                atol=BF16_ON_LOAD_ATOL)
+    assert agreement >= BF16_ON_LOAD_MIN_AGREEMENT
+    assert report.max_abs <= BF16_ON_LOAD_ATOL
 
 
-def test_v4096_d512_l6_batch256_greedy_bf16_weights(runtime, tmp_path):
-    w = config("v4096-d512-l6-w512-b256-greedy-bf16w")
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
-    W, V = w.model.window, w.model.vocabulary
-    ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, V), W, V)
-    tokens = engine.generateBatch(ctx, w.steps)
-    check_points(engine, oracle, ctx, tokens, [(3, 0), (200, 200), (255, 255)], W)
+def test_v8192_d768_l12_batch1_greedy_bf16_weights_every_step(runtime, tmp_path):
+    # The single-stream workload: 512-token prompt, all 512 greedy steps through the fused step.
+    greedy_full(runtime, tmp_path, "v8192-d768-l12-w1024-b1-greedy-bf16w", [0])
 
 
-def test_v8192_d768_l12_batch1_greedy_bf16_weights(runtime, tmp_path):
-    w = config("v8192-d768-l12-w1024-b1-greedy-bf16w")
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
-    W, V = w.model.window, w.model.vocabulary
-    ctx = left_pad(synthetic_prompts(w.prompt_seed, 1, w.prompt, V), W, V)
-    tokens = engine.generateBatch(ctx, w.steps)
-    check_points(engine, oracle, ctx, tokens, [(0, 0), (0, 256), (0, 511)], W)
-
-
-def test_v8192_d768_l12_sampled_rows_of_the_8192_sequence_run(runtime, tmp_path):
-    # The 8192-sequence streamSampled workload (T = 1.0, seed 9): its first 64 rows, decoded in
-    # waves of 32, draw what the first 64 successive calls of the full run draw. Draws are
-    # replayed against the oracle at sampled steps from the skip-ahead generator state.
-    from dataclasses import replace
-
-    from parity import draw_margin
-
+def test_v8192_d768_l12_8192_sequences_sampled_every_draw(runtime, tmp_path):
+    # The 8192-sequence streamSampled workload (T = 1.0, seed 9, 512 tokens) in waves of 1024
+    # rows: rows from four different waves are replayed draw for draw, each from the generator
+    # state one engine seeded once would hold at its first draw (TextEngine.java:43,417).
     w = config("v8192-d768-l12-w1024-n8192-sampled-bf16w")
-    m = replace(w.model, max_rows=32)
-    w = replace(w, model=m, rows=64, steps=48)
+    m = w.model
     engine, oracle = pair(runtime, w, tmp_path / "w.bin")
-    W, V = m.window, m.vocabulary
-    ctx = left_pad(synthetic_prompts(w.prompt_seed, 64, w.prompt, V), W, V)
+    ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
+                   m.vocabulary)
+    rows = [0, 1500, 4100, 8191]
     engine.seed(w.sample_seed)
-    tokens = engine.sampleBatch(ctx, w.steps, w.temperature, w.k)
-    start = orc.lcg_scramble(w.sample_seed)
-    for r, g in [(0, 0), (0, 47), (31, 20), (32, 5), (63, 47)]:
-        state = orc.lcg_advance(start, 2 * w.steps * r + 2 * g)
-        ref = oracle.scores(window_at(ctx[r], tokens[r], g, W))
-        want, margin, _ = draw_margin(ref, w.temperature, w.k, state)
-        assert want == tokens[r, g] or margin < 1e-4, (r, g, tokens[r, g], want)
+    tokens, logits = engine.sampleWithLogitsOf(ctx, w.steps, w.temperature, w.k, rows)
+    assert tokens.shape == (8192, 512) and tokens.min() >= 0 and tokens.max() < m.vocabulary
+    states = [shard_rng_state(w.sample_seed, w.steps, r) for r in rows]
+    report = Report()
+    _, agreement = check_rows(oracle, ctx, rows, tokens[rows], logits, report, "c5",
+                              sampled=(w.temperature, w.k, states))
+    report_line("v8192-d768-l12-n8192-sampled", report, agreement, rows=rows)
+    assert_clean(report, rows)
+    # A batch shard (the second half, as rank 1 of 2 decodes it) draws the same tokens.
+    first = 4096
+    engine.rng_state = shard_rng_state(w.sample_seed, w.steps, first)
+    shard = engine.sampleBatch(ctx[first:], w.steps, w.temperature, w.k)
+    np.testing.assert_array_equal(shard, tokens[first:])
 
 
 def test_v8192_d768_l12_512_rows_greedy_bf16_weights(runtime, tmp_path):
     # 512 rows (two lanes of 256) of the 8192-sequence run's architecture: its decode projections
     # have between one and two work units per SM (e.g. the QKV GEMM: 72 tiles x 3 splits), the
     # case served by the two-CTAs-per-SM ring of the one-tile GEMM.
-    from dataclasses import replace
-
     w = config("v8192-d768-l12-w1024-n8192-sampled-bf16w")
     m = replace(w.model, max_rows=0)
-    w = replace(w, model=m, rows=512, steps=4, mode="greedy")
+    w = replace(w, model=m, rows=512, steps=8, mode="greedy")
     engine, oracle = pair(runtime, w, tmp_path / "w.bin")
-    W, V = m.window, m.vocabulary
-    ctx = left_pad(synthetic_prompts(w.prompt_seed, 512, w.prompt, V), W, V)
-    tokens = engine.generateBatch(ctx, w.steps)
-    assert tokens.shape == (512, 4) and tokens.min() >= 0 and tokens.max() < V
-    check_points(engine, oracle, ctx, tokens, [(0, 0), (300, 3), (511, 3)], W)
+    ctx = left_pad(synthetic_prompts(w.prompt_seed, 512, w.prompt, m.vocabulary), m.window,
+                   m.vocabulary)
+    rows = [0, 255, 256, 511]
+    tokens, logits = engine.generateWithLogitsOf(ctx, w.steps, rows)
+    np.testing.assert_array_equal(tokens, engine.generateBatch(ctx, w.steps))
+    report = Report()
+    _, agreement = check_rows(oracle, ctx, rows, tokens[rows], logits, report, "512 rows")
+    report_line("v8192-d768-l12-512-rows", report, agreement, rows=rows)
+    assert_clean(report, rows)

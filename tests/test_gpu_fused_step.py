@@ -136,3 +136,33 @@ def test_stock_decoder_family_never_uses_the_cache_step(runtime, tmp_path):
     for r in range(2):
         check_greedy_row(oracle, ctx[r], tokens[r], logits[r], report, f"row{r}")
     assert not report.mismatches
+
+
+@pytest.mark.parametrize("code,words", [(11, "grid barrier"), (12, "weight staging"),
+                                        (3, "tensor-core GEMM")])
+def test_a_recorded_pipeline_error_stops_the_run_before_the_sink(runtime, tmp_path, code, words):
+    # Host-side injection: the run's status word starts out set, as a kernel that gave up on a
+    # bounded wait leaves it (no kernel is made to fail). Every fused step of the run then returns
+    # at entry, the call fails with BST_PANIC after the first step, the token sink never sees a
+    # token, and the engine decodes normally afterwards.
+    import time
+
+    from basalt_b200 import BasaltRuntimeException
+
+    spec = ModelSpec("padded_decoder", 96, 64, 128, 2, 4, 512)
+    engine, oracle = make_pair(runtime, spec, tmp_path / "w.bin")
+    ctx = left_pad(synthetic_prompts(1, 1, 16, 96), 64, 96)
+    want = oracle.generate(ctx[0], 48)
+    seen = []
+    os.environ["BST_INJECT_PIPELINE_ERROR"] = str(code)
+    try:
+        start = time.perf_counter()
+        with pytest.raises(BasaltRuntimeException) as info:
+            engine.stream(ctx[0], 48, seen.append)
+        elapsed = time.perf_counter() - start
+    finally:
+        del os.environ["BST_INJECT_PIPELINE_ERROR"]
+    assert info.value.code == -6 and words in str(info.value)
+    assert seen == []
+    assert elapsed < 5.0
+    np.testing.assert_array_equal(engine.generate(ctx[0], 48), want)

@@ -319,3 +319,62 @@ def test_cached_decode_serves_the_padded_decoder_only():
     e = _tiny_decoder(orc.FAMILY_DECODER)
     with pytest.raises(Exception, match="padded decoder"):
         e.generate_batch_cached(np.zeros((1, 10), dtype=np.int32), 2)
+
+
+def test_single_pass_forced_logits_agree_with_per_step_recompute():
+    # The one-pass teacher-forced logits (used at full size) against TextEngine's recompute of
+    # every step's window, on a model small enough for the recompute.
+    e = orc.OracleEngine(orc.FAMILY_PADDED_DECODER, 96, 64, 128, 2, 4, 512)
+    rng = np.random.default_rng(3)
+    for name, size in e.parameters():
+        if "norm" in name:
+            base = 1.0 if name.endswith("gamma") else 0.0
+            e.set(name, (base + 0.2 * rng.standard_normal(size)).astype(np.float32))
+        else:
+            e.set(name, (0.05 * rng.standard_normal(size)).astype(np.float32))
+    ctx = orc.left_pad(orc.synthetic_prompts(1, 3, 16, 96), 64, 96)
+    forced = rng.integers(0, 96, size=(3, 40)).astype(np.int32)
+    one_pass = e.forced_scores_rows(ctx, forced)
+    for r in range(3):
+        per_step = e.forced_scores(ctx[r], forced[r])
+        np.testing.assert_allclose(one_pass[r], per_step, atol=1e-5, rtol=1e-5)
+    # A window that would drop a real token falls back to the per-step recompute.
+    long = rng.integers(0, 96, size=(1, 60)).astype(np.int32)
+    full = e.forced_scores_rows(orc.left_pad(long, 64, 96), forced[:1])
+    np.testing.assert_array_equal(full[0], e.forced_scores(orc.left_pad(long, 64, 96)[0],
+                                                           forced[0]))
+
+
+def test_vectorised_draw_replay_matches_the_oracle_draw():
+    from parity import draw_margin
+
+    e = orc.OracleEngine(orc.FAMILY_LAST_TOKEN, 300, 4)
+    rng = np.random.default_rng(5)
+    for trial in range(50):
+        scores = rng.standard_normal(300) * (0.1 if trial % 2 else 3.0)
+        if trial % 5 == 0:
+            scores[rng.integers(0, 300, 20)] = scores[0]  # ties keep index order
+        temperature = float(rng.choice([0.3, 0.8, 1.0, 2.5]))
+        top_k = int(rng.choice([1, 7, 300]))
+        e.seed(trial)
+        state = e.rng_state
+        want = e.draw(scores, temperature, top_k)
+        token, _, after = draw_margin(scores, temperature, top_k, state)
+        assert token == want
+        assert after == e.rng_state
+
+
+def test_oracle_synthetic_inputs_match_the_library_writer(tmp_path):
+    # The CPU baseline generates its weights and prompts without the CUDA library; they must be
+    # the files and ids the engine is benchmarked on.
+    from dataclasses import replace
+
+    from basalt_b200 import config, synthetic_prompts, write_synthetic_weights
+
+    model = config("v96-d256-l4-w128-b32-greedy").model
+    for m in (model, replace(model, weight_dtype="bf16")):
+        orc.write_synthetic_weights(m, tmp_path / "o.bin", 0)
+        write_synthetic_weights(m, tmp_path / "g.bin", 0)
+        assert (tmp_path / "o.bin").read_bytes() == (tmp_path / "g.bin").read_bytes()
+    np.testing.assert_array_equal(orc.synthetic_prompts(3, 5, 40, 4096),
+                                  synthetic_prompts(3, 5, 40, 4096))
