@@ -105,6 +105,25 @@ SIGNATURES = {
     "bst_matmul_static": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                            ctypes.c_int64, ctypes.c_int64]),
+    "bst_recognize_model": (ctypes.c_int32, [_P(ctypes.c_char_p), _i32p, _i64p, ctypes.c_int32,
+                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                             _P(ModelSpecStruct)]),
+    "bst_engine_create_from_parameters": (ctypes.c_int32, [
+        _P(ctypes.c_char_p), _i32p, _i64p, _P(_f32p), ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+        _P(_u64)]),
+    "bst_context_create": (ctypes.c_int32, [ctypes.c_int32, _P(_u64)]),
+    "bst_context_destroy": (ctypes.c_int32, [_u64]),
+    "bst_tensor_create": (ctypes.c_int32, [_u64, ctypes.c_int32, _i64p, ctypes.c_int32, _f32p,
+                                           _P(_u64)]),
+    "bst_tensor_transfer": (ctypes.c_int32, [_u64, _u64, ctypes.c_int32, _P(_u64)]),
+    "bst_tensor_read": (ctypes.c_int32, [_u64, _u64, _f32p, ctypes.c_int64]),
+    "bst_tensor_write": (ctypes.c_int32, [_u64, _u64, _f32p, ctypes.c_int64]),
+    "bst_tensor_info": (ctypes.c_int32, [_u64, _u64, _i32p, _i32p, _i64p, ctypes.c_int32]),
+    "bst_tensor_release": (ctypes.c_int32, [_u64, _u64, _i32p]),
+    "bst_execute_queue": (ctypes.c_int32, [_u64, ctypes.c_void_p, ctypes.c_int32]),
+    "bst_context_stats": (ctypes.c_int32, [_u64, _i64p]),
+    "bst_context_clear_graph": (ctypes.c_int32, [_u64]),
     "bst_last_error": (ctypes.c_int32, [_u64, ctypes.c_char_p, ctypes.c_int32]),
     "bst_write_synthetic_weights": (ctypes.c_int32, [_P(ModelSpecStruct), ctypes.c_char_p,
                                                      ctypes.c_int64, ctypes.c_double]),

@@ -20,7 +20,8 @@ LIBRARY = PACKAGE / "libbasalt_cuda.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", str(INCLUDE),
           "-I", str(CSRC)]
-SOURCES = ["kernels.cu", "gemm_tc.cu", "decode_fused.cu", "ops.cu", "ops_static.cu", "engine.cpp"]
+SOURCES = ["kernels.cu", "gemm_tc.cu", "decode_fused.cu", "ops.cu", "ops_static.cu", "tensors.cu",
+           "engine.cpp"]
 HEADERS = ["kernels.h", "java_random.h", "epilogue.cuh", "device.cuh", "select.cuh"]
 
 

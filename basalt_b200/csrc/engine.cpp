@@ -171,6 +171,142 @@ Failure validate_spec(const bst_model_spec& s) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Recognising a module from its namedParameters (torch/Module.java:27-34): the names, in order,
+// and the shapes in the reference's layout (Linear weights [in, out], biases [1, out], LayerNorm
+// parameters [d], Embedding tables [rows, d]).
+// ---------------------------------------------------------------------------------------------
+struct ParamView {
+    std::string name;
+    std::vector<int64_t> dims;
+    int64_t numel() const {
+        int64_t n = 1;
+        for (int64_t x : dims) n *= x;
+        return n;
+    }
+    bool is(int64_t a, int64_t b) const { return dims.size() == 2 && dims[0] == a && dims[1] == b; }
+};
+
+Failure recognize(const std::vector<ParamView>& params, int vocabulary, int window, int heads,
+                  bst_model_spec* out) {
+    bst_model_spec s{};
+    s.vocabulary = vocabulary;
+    s.window = window;
+    s.heads = 1;
+    auto find = [&](const std::string& n) -> const ParamView* {
+        for (const auto& p : params) {
+            if (p.name == n) return &p;
+        }
+        return nullptr;
+    };
+    const Failure unsupported{BST_UNSUPPORTED,
+                              "the module is not one of the served language models (a "
+                              "TransformerBlock decoder with token and position embeddings, "
+                              "Zoo.charLm, or a one-hot last-token head)"};
+    const ParamView* emb = find("embedding.weight");
+    const ParamView* pos = find("position.weight");
+    const ParamView* head = find("head.weight");
+    const ParamView* ffn1 = find("layer0.ffn1.weight");
+    if (emb && pos && head && ffn1) {
+        if (pos->dims.size() != 2 || head->dims.size() != 2 || emb->dims.size() != 2 ||
+            ffn1->dims.size() != 2) {
+            return {BST_SHAPE, "decoder matrices must be rank 2"};
+        }
+        const int64_t d = pos->dims[1];
+        if (pos->dims[0] != window) {
+            return {BST_SHAPE, "position.weight has " + std::to_string(pos->dims[0]) +
+                                   " rows; the window is " + std::to_string(window)};
+        }
+        if (!head->is(d, vocabulary)) {
+            return {BST_SHAPE, "head.weight must be [" + std::to_string(d) + ", " +
+                                   std::to_string(vocabulary) + "]"};
+        }
+        if (emb->is(vocabulary + 1, d)) {
+            s.family = BST_FAMILY_PADDED_DECODER;  // the extra row is PAD = vocabulary
+        } else if (emb->is(vocabulary, d)) {
+            s.family = BST_FAMILY_DECODER;
+        } else {
+            return {BST_SHAPE, "embedding.weight must be [" + std::to_string(vocabulary) + " or " +
+                                   std::to_string(vocabulary + 1) + ", " + std::to_string(d) + "]"};
+        }
+        int layers = 0;
+        while (find("layer" + std::to_string(layers) + ".norm1.gamma")) ++layers;
+        if (heads < 1) {
+            return {BST_INVALID, "the head count of a decoder must be given: MultiheadAttention's "
+                                 "parameter shapes do not carry it"};
+        }
+        s.dimension = static_cast<int32_t>(d);
+        s.layers = layers;
+        s.heads = heads;
+        s.hidden = static_cast<int32_t>(ffn1->dims[1]);
+    } else if (params.size() == 7 && find("param0") && find("param6")) {
+        // Zoo.charLm: embedding [V, d], expand [W d, h] + [1, h], contract [h, W d] + [1, W d],
+        // head [W d, V] + [1, V] (zoo/Zoo.java:135-168).
+        const ParamView& e0 = params[0];
+        const ParamView& e1 = params[1];
+        if (e0.dims.size() != 2 || e1.dims.size() != 2 || e0.dims[0] != vocabulary) return unsupported;
+        s.family = BST_FAMILY_CHAR_LM;
+        s.dimension = static_cast<int32_t>(e0.dims[1]);
+        s.hidden = static_cast<int32_t>(e1.dims[1]);
+        if (e1.dims[0] != static_cast<int64_t>(window) * s.dimension) {
+            return {BST_SHAPE, "charLm expand weight must have window x dimension = " +
+                                   std::to_string(static_cast<int64_t>(window) * s.dimension) +
+                                   " rows"};
+        }
+    } else if (params.size() == 2 && params[0].name == "param0" && params[1].name == "param1" &&
+               params[0].is(vocabulary, vocabulary) && params[1].numel() == vocabulary) {
+        s.family = BST_FAMILY_LAST_TOKEN;  // TextEngineTest.LastTokenModel (Linear(V, V))
+    } else {
+        return unsupported;
+    }
+    const Failure f = validate_spec(s);
+    if (f.code) return f;
+    // Every parameter of the recognised architecture, by name, in order, with its element count.
+    std::vector<std::string> names;
+    std::vector<int64_t> sizes;
+    declare_parameters(s, &names, &sizes);
+    if (names.size() != params.size()) {
+        return {BST_SHAPE, "the module has " + std::to_string(params.size()) +
+                               " parameters; the recognised architecture has " +
+                               std::to_string(names.size())};
+    }
+    for (size_t i = 0; i < names.size(); ++i) {
+        if (params[i].name != names[i]) {
+            return {BST_SHAPE, "parameter " + std::to_string(i) + " is " + params[i].name +
+                                   ", expected " + names[i]};
+        }
+        if (params[i].numel() != sizes[i]) {
+            return {BST_SHAPE, "parameter " + names[i] + " has " +
+                                   std::to_string(params[i].numel()) + " values, expected " +
+                                   std::to_string(sizes[i])};
+        }
+    }
+    *out = s;
+    return {BST_OK, ""};
+}
+
+Failure parameter_views(const char* const* names, const int32_t* ranks, const int64_t* dims,
+                        int32_t count, std::vector<ParamView>* out) {
+    if (count < 1 || !names || !ranks || !dims) {
+        return {BST_INVALID, "names, ranks and dims must describe at least one parameter"};
+    }
+    size_t at = 0;
+    for (int32_t i = 0; i < count; ++i) {
+        if (!names[i]) return {BST_INVALID, "parameter name " + std::to_string(i) + " is null"};
+        if (ranks[i] < 1 || ranks[i] > 8) {
+            return {BST_SHAPE, std::string("parameter ") + names[i] + " has rank " +
+                                   std::to_string(ranks[i])};
+        }
+        ParamView v{names[i], std::vector<int64_t>(dims + at, dims + at + ranks[i])};
+        at += static_cast<size_t>(ranks[i]);
+        for (int64_t x : v.dims) {
+            if (x < 0) return {BST_SHAPE, std::string("parameter ") + names[i] + " has a negative dimension"};
+        }
+        out->push_back(std::move(v));
+    }
+    return {BST_OK, ""};
+}
+
+// ---------------------------------------------------------------------------------------------
 // TextEngine weight file (TextEngine.java:298-350): big-endian int V, int W, int count, then per
 // parameter DataOutputStream.writeUTF(name), int n, n floats.
 // ---------------------------------------------------------------------------------------------
@@ -1898,6 +2034,62 @@ int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine
         std::lock_guard<std::mutex> lock(g_registry_mutex);
         const uint64_t h = g_next_handle++;
         g_engines[h] = e;
+        *out = h;
+        return BST_OK;
+    })
+}
+
+int32_t bst_recognize_model(const char* const* names, const int32_t* ranks, const int64_t* dims,
+                            int32_t count, int32_t vocabulary, int32_t window, int32_t heads,
+                            bst_model_spec* spec) {
+    BST_GUARDED({
+        if (!spec) {
+            t_last_error = "spec must not be null";
+            return BST_INVALID;
+        }
+        std::vector<ParamView> params;
+        Failure f = parameter_views(names, ranks, dims, count, &params);
+        if (!f.code) f = recognize(params, vocabulary, window, heads, spec);
+        if (f.code) t_last_error = f.message;
+        return f.code;
+    })
+}
+
+int32_t bst_engine_create_from_parameters(const char* const* names, const int32_t* ranks,
+                                          const int64_t* dims, const float* const* values,
+                                          int32_t count, int32_t vocabulary, int32_t window,
+                                          int32_t heads, int32_t weight_dtype, int32_t kv_dtype,
+                                          int32_t device, bst_engine* out) {
+    BST_GUARDED({
+        if (!out || !values) {
+            t_last_error = "values and out must not be null";
+            return BST_INVALID;
+        }
+        bst_model_spec spec{};
+        int32_t st = bst_recognize_model(names, ranks, dims, count, vocabulary, window, heads, &spec);
+        if (st) return st;
+        spec.weight_dtype = weight_dtype;
+        spec.kv_dtype = kv_dtype;
+        std::vector<ParamView> params;
+        parameter_views(names, ranks, dims, count, &params);
+        for (int32_t i = 0; i < count; ++i) {
+            if (!values[i] && params[i].numel() > 0) {
+                t_last_error = "values of parameter " + params[i].name + " are null";
+                return BST_INVALID;
+            }
+        }
+        bst_engine h = 0;
+        st = bst_engine_create(&spec, device, &h);
+        if (st) return st;
+        for (int32_t i = 0; i < count; ++i) {
+            st = bst_set_parameter(h, names[i], values[i], params[i].numel());
+            if (st) {
+                const std::string why = t_last_error;
+                bst_engine_destroy(h);
+                t_last_error = why;
+                return st;
+            }
+        }
         *out = h;
         return BST_OK;
     })

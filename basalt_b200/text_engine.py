@@ -194,6 +194,27 @@ class TextEngine:
         _raise(lib.bst_engine_create(ctypes.byref(spec), runtime.device, ctypes.byref(handle)))
         return TextEngine(runtime, model, handle.value)
 
+    @staticmethod
+    def ofParameters(runtime: Basalt, named_parameters, vocabulary: int, window: int,
+                     heads: int = 0, weight_dtype: str = "f32",
+                     kv_dtype: str = "f32") -> "TextEngine":
+        """TextEngine.of on a module given by its namedParameters: (name, array) pairs in the
+        module's order, arrays in the reference's layout. Raises
+        BasaltUnsupportedOperationException for a module the engine does not serve."""
+        lib = _lib.load()
+        args = _parameter_arrays(named_parameters)
+        values = [np.ascontiguousarray(v, dtype=np.float32) for _, v in named_parameters]
+        ptrs = (_lib._f32p * len(values))(*[v.ctypes.data_as(_lib._f32p) for v in values])
+        handle = ctypes.c_uint64(0)
+        _raise(lib.bst_engine_create_from_parameters(
+            args[0], args[1], args[2], ptrs, len(values), vocabulary, window, heads,
+            DTYPES[weight_dtype], DTYPES[kv_dtype], runtime.device, ctypes.byref(handle)))
+        model = recognize_model(named_parameters, vocabulary, window, heads)
+        from dataclasses import replace
+
+        model = replace(model, weight_dtype=weight_dtype, kv_dtype=kv_dtype)
+        return TextEngine(runtime, model, handle.value)
+
     def vocabulary(self) -> int:
         return self._model.vocabulary
 
@@ -524,6 +545,28 @@ class TextEngine:
             raise errors[0]
         self._call(code)
         return out
+
+
+def _parameter_arrays(named_parameters):
+    names = [n.encode() for n, _ in named_parameters]
+    shapes = [np.shape(v) for _, v in named_parameters]
+    c_names = (ctypes.c_char_p * len(names))(*names)
+    ranks = (ctypes.c_int32 * len(shapes))(*[len(s) for s in shapes])
+    flat = [int(x) for s in shapes for x in s]
+    dims = (ctypes.c_int64 * max(1, len(flat)))(*flat)
+    return c_names, ranks, dims
+
+
+def recognize_model(named_parameters, vocabulary: int, window: int, heads: int = 0) -> ModelSpec:
+    """The architecture the engine serves for a module with these namedParameters (name, array)
+    pairs, or BasaltUnsupportedOperationException: the decision TextEngine's dispatch makes."""
+    names, ranks, dims = _parameter_arrays(named_parameters)
+    spec = _lib.ModelSpecStruct()
+    _raise(_lib.load().bst_recognize_model(names, ranks, dims, len(named_parameters), vocabulary,
+                                           window, heads, ctypes.byref(spec)))
+    family = {v: k for k, v in FAMILIES.items()}[spec.family]
+    return ModelSpec(family, spec.vocabulary, spec.window, spec.dimension, spec.layers, spec.heads,
+                     spec.hidden)
 
 
 def write_synthetic_weights(model: ModelSpec, path, seed: int, stddev: float = 0.02):

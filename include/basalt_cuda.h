@@ -80,6 +80,27 @@ int32_t bst_device_count(int32_t* count);
 int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine* out);
 int32_t bst_engine_destroy(bst_engine engine);
 
+/* Recognition of a module by its namedParameters (torch/Module.java:27-34), the test TextEngine's
+ * dispatch makes before it hands a module to this engine. `count` parameters: names[i] with
+ * ranks[i] dimensions, all dimensions concatenated in `dims`, in the reference's layout (Linear
+ * weight [in, out], bias [1, out]; LayerNorm gamma/beta [d]; Embedding [rows, d]). vocabulary and
+ * window are TextEngine.of's arguments (TextEngine.java:61-74); heads is the decoder's head count
+ * (MultiheadAttention's parameter shapes do not carry it; ignored otherwise). Recognised: the
+ * padded decoder (embedding rows V + 1) and the stock decoder (V rows), Zoo.charLm
+ * (zoo/Zoo.java:135-168) and the one-hot last-token head (TextEngineTest.java:210-243). Fills
+ * `spec` (f32 storage, max_rows 0) or returns BST_UNSUPPORTED / BST_SHAPE with the reason. */
+int32_t bst_recognize_model(const char* const* names, const int32_t* ranks, const int64_t* dims,
+                            int32_t count, int32_t vocabulary, int32_t window, int32_t heads,
+                            bst_model_spec* spec);
+/* TextEngine.of(module, vocabulary, window) for a recognised module: creates the engine on
+ * `device` with the given storage dtypes and copies every parameter by name
+ * (Module.loadStateDict, torch/Module.java:68-76). values[i] holds parameter i's floats. */
+int32_t bst_engine_create_from_parameters(const char* const* names, const int32_t* ranks,
+                                          const int64_t* dims, const float* const* values,
+                                          int32_t count, int32_t vocabulary, int32_t window,
+                                          int32_t heads, int32_t weight_dtype, int32_t kv_dtype,
+                                          int32_t device, bst_engine* out);
+
 /* Parameters by name, in Module.namedParameters order (torch/Module.java:27-34). */
 int32_t bst_parameter_count(bst_engine engine, int32_t* count);
 int32_t bst_parameter_info(bst_engine engine, int32_t index, char* name, int32_t capacity,
@@ -186,6 +207,51 @@ int32_t bst_matmul(int32_t device, void* stream, const float* a, const float* b,
  * on the GPU races, so such calls must be serialised by the caller. */
 int32_t bst_matmul_static(int32_t device, void* stream, const float* a, const float* b, float* c,
                           int64_t m, int64_t k, int64_t n);
+
+/* ---- Device tensors and the op queue (NativeContext on Device.cuda(i)) ----
+ * A context is bound to one CUDA device. Its tensors live on that device (device tag 1000 + i,
+ * Device.java:22,46-59) or on the host (tag 0). Tensor handles are monotonic per context and never
+ * reused (native/src/tensor.rs:150-176). Ops run from the reference's packed queue of 128-byte
+ * commands (CommandQueueBuilder.java:12-73): u8 op code, u8 flags, 6 pad, u64 inputs A..E, u64
+ * output, i32 attrs[16], 8 reserved. Codes run on the GPU: MatMul 1, Add 2, ReLU 3, Sub 4, Mul 5,
+ * Sigmoid 6, Tanh 7, Gelu 11, Exp 23, Log 24, Sqrt 25, Abs 26, Neg 27, Div 28 (binary ops broadcast
+ * trailing axes as ops.rs:136-164); other codes return BST_UNSUPPORTED. Each executed op is
+ * recorded as one graph node, as the reference's Graph::push does; no backward is offered. */
+typedef uint64_t bst_context;
+typedef uint64_t bst_tensor;
+#define BST_DEVICE_TAG_CPU 0
+#define BST_DEVICE_TAG_CUDA 1000
+#define BST_COMMAND_BYTES 128
+
+/* NativeContext.create for Device.cuda(i): device_tag = 1000 + i. Tag 0 (cpu) returns
+ * BST_UNSUPPORTED: host contexts stay on the CPU engine. */
+int32_t bst_context_create(int32_t device_tag, bst_context* out);
+int32_t bst_context_destroy(bst_context context);
+/* NativeContext.of / zeros (values NULL: zeros) on the device named by device_tag (0 or this
+ * context's 1000 + i). */
+int32_t bst_tensor_create(bst_context context, int32_t device_tag, const int64_t* shape,
+                          int32_t rank, const float* values, bst_tensor* out);
+/* NativeContext.transferTensor (native/src/context.rs:125-133): a copy on the target device, as
+ * a new handle; host <-> device transfers are cudaMemcpy on the context's stream. */
+int32_t bst_tensor_transfer(bst_context context, bst_tensor source, int32_t device_tag,
+                            bst_tensor* out);
+/* NativeTensorHandle.data / setData: count must equal the tensor's element count. */
+int32_t bst_tensor_read(bst_context context, bst_tensor tensor, float* values, int64_t count);
+int32_t bst_tensor_write(bst_context context, bst_tensor tensor, const float* values,
+                         int64_t count);
+/* Device tag, rank and up to `capacity` dimensions of a tensor. */
+int32_t bst_tensor_info(bst_context context, bst_tensor tensor, int32_t* device_tag,
+                        int32_t* rank, int64_t* shape, int32_t capacity);
+/* NativeTensorHandle.close: releasing twice is harmless (*released 0 the second time); a handle
+ * the context never issued returns BST_UNKNOWN_HANDLE. */
+int32_t bst_tensor_release(bst_context context, bst_tensor tensor, int32_t* released);
+/* NativeBindings.executeQueue (native/src/engine.rs:118-154): runs `count` commands in order and
+ * returns once they have finished; the first failing command stops the queue with its status. */
+int32_t bst_execute_queue(bst_context context, const void* commands, int32_t count);
+/* out[0] live tensors, out[1] live device bytes, out[2] graph nodes (NativeContext.graphSize),
+ * out[3] kernels launched. */
+int32_t bst_context_stats(bst_context context, int64_t out[4]);
+int32_t bst_context_clear_graph(bst_context context);
 
 /* Message of the last failure on this engine (engine 0: on this thread). */
 int32_t bst_last_error(bst_engine engine, char* buffer, int32_t capacity);

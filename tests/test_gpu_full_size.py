@@ -34,9 +34,27 @@ BF16_ON_LOAD_ATOL = 5e-2
 BF16_ON_LOAD_MIN_AGREEMENT = 0.95
 
 
-def pair(runtime, workload, path, engine_model=None):
+@pytest.fixture(scope="module")
+def weights(tmp_path_factory):
+    """One synthetic weight file per architecture for the module (the 85 M-parameter model takes
+    tens of seconds to draw)."""
+    cache = {}
+    folder = tmp_path_factory.mktemp("weights")
+
+    def get(model, seed):
+        key = (model.vocabulary, model.window, model.dimension, model.layers, model.heads,
+               model.hidden, model.weight_dtype, seed)
+        if key not in cache:
+            cache[key] = folder / f"w{len(cache)}.bin"
+            write_synthetic_weights(model, cache[key], seed)
+        return cache[key]
+
+    return get
+
+
+def pair(runtime, workload, weights, engine_model=None):
     m = workload.model
-    write_synthetic_weights(m, path, workload.weight_seed)
+    path = weights(m, workload.weight_seed)
     em = engine_model or m
     engine = TextEngine.of(runtime, em, em.vocabulary, em.window)
     engine.load(path)
@@ -58,9 +76,9 @@ def assert_clean(report, rows):
     assert len(report.near_ties) <= len(rows), report.near_ties
 
 
-def greedy_full(runtime, tmp_path, name, rows):
+def greedy_full(runtime, weights, name, rows):
     w = config(name)
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
+    engine, oracle = pair(runtime, w, weights)
     m = w.model
     ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
                    m.vocabulary)
@@ -74,22 +92,22 @@ def greedy_full(runtime, tmp_path, name, rows):
     return engine, ctx, tokens
 
 
-def test_v4096_d512_l6_batch256_greedy_every_step(runtime, tmp_path):
+def test_v4096_d512_l6_batch256_greedy_every_step(runtime, weights):
     # Rows from both decode lanes (0..127 and 128..255), all 256 steps.
-    greedy_full(runtime, tmp_path, "v4096-d512-l6-w512-b256-greedy",
+    greedy_full(runtime, weights, "v4096-d512-l6-w512-b256-greedy",
                 [0, 63, 127, 128, 191, 255])
 
 
-def test_v4096_d512_l6_batch256_greedy_bf16_weights_every_step(runtime, tmp_path):
-    greedy_full(runtime, tmp_path, "v4096-d512-l6-w512-b256-greedy-bf16w", [0, 127, 128, 255])
+def test_v4096_d512_l6_batch256_greedy_bf16_weights_every_step(runtime, weights):
+    greedy_full(runtime, weights, "v4096-d512-l6-w512-b256-greedy-bf16w", [0, 127, 128, 255])
 
 
-def test_v4096_d512_l6_bf16_conversion_on_load_agreement(runtime, tmp_path):
+def test_v4096_d512_l6_bf16_conversion_on_load_agreement(runtime, weights):
     # The fp32 weight file into an engine that stores bf16 matrices (TextEngine.load keeps the
     # file's fp32 values; the device store rounds them to bf16), against the fp32 oracle.
     w = config("v4096-d512-l6-w512-b256-greedy")
     m = w.model
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin", replace(m, weight_dtype="bf16"))
+    engine, oracle = pair(runtime, w, weights, replace(m, weight_dtype="bf16"))
     rows = [0, 100, 200, 255]
     ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
                    m.vocabulary)
@@ -103,18 +121,18 @@ def test_v4096_d512_l6_bf16_conversion_on_load_agreement(runtime, tmp_path):
     assert report.max_abs <= BF16_ON_LOAD_ATOL
 
 
-def test_v8192_d768_l12_batch1_greedy_bf16_weights_every_step(runtime, tmp_path):
+def test_v8192_d768_l12_batch1_greedy_bf16_weights_every_step(runtime, weights):
     # The single-stream workload: 512-token prompt, all 512 greedy steps through the fused step.
-    greedy_full(runtime, tmp_path, "v8192-d768-l12-w1024-b1-greedy-bf16w", [0])
+    greedy_full(runtime, weights, "v8192-d768-l12-w1024-b1-greedy-bf16w", [0])
 
 
-def test_v8192_d768_l12_8192_sequences_sampled_every_draw(runtime, tmp_path):
+def test_v8192_d768_l12_8192_sequences_sampled_every_draw(runtime, weights):
     # The 8192-sequence streamSampled workload (T = 1.0, seed 9, 512 tokens) in waves of 1024
     # rows: rows from four different waves are replayed draw for draw, each from the generator
     # state one engine seeded once would hold at its first draw (TextEngine.java:43,417).
     w = config("v8192-d768-l12-w1024-n8192-sampled-bf16w")
     m = w.model
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
+    engine, oracle = pair(runtime, w, weights)
     ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
                    m.vocabulary)
     rows = [0, 1500, 4100, 8191]
@@ -134,14 +152,14 @@ def test_v8192_d768_l12_8192_sequences_sampled_every_draw(runtime, tmp_path):
     np.testing.assert_array_equal(shard, tokens[first:])
 
 
-def test_v8192_d768_l12_512_rows_greedy_bf16_weights(runtime, tmp_path):
+def test_v8192_d768_l12_512_rows_greedy_bf16_weights(runtime, weights):
     # 512 rows (two lanes of 256) of the 8192-sequence run's architecture: its decode projections
     # have between one and two work units per SM (e.g. the QKV GEMM: 72 tiles x 3 splits), the
     # case served by the two-CTAs-per-SM ring of the one-tile GEMM.
     w = config("v8192-d768-l12-w1024-n8192-sampled-bf16w")
     m = replace(w.model, max_rows=0)
     w = replace(w, model=m, rows=512, steps=8, mode="greedy")
-    engine, oracle = pair(runtime, w, tmp_path / "w.bin")
+    engine, oracle = pair(runtime, w, weights)
     ctx = left_pad(synthetic_prompts(w.prompt_seed, 512, w.prompt, m.vocabulary), m.window,
                    m.vocabulary)
     rows = [0, 255, 256, 511]
