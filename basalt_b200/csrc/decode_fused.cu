@@ -304,15 +304,6 @@ struct Sink {
     unsigned long long* best = nullptr;  // kLogits: per-row packed maximum (shared)
 };
 
-// Orders floats as unsigned integers (ascending), +0 and -0 equal; the low word prefers the
-// smaller index, so the packed maximum is TextEngine.argmax's first maximum.
-__device__ __forceinline__ unsigned long long pack_best(float v, int idx) {
-    if (v == 0.0f) v = 0.0f;
-    const unsigned b = __float_as_uint(v);
-    const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    return (static_cast<unsigned long long>(ord) << 32) | (0xffffffffu - static_cast<unsigned>(idx));
-}
-
 // One output of a projection through its epilogue (chosen at run time).
 __device__ __forceinline__ void store_out(Epi epi, const EpiArgs& ea, const Sink& sk, int c0, int m,
                                        int n, float v) {

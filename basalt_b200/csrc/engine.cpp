@@ -524,6 +524,9 @@ class Engine {
     // every row. hist_count: rows of the current wave whose logits are stashed.
     std::vector<int32_t> watch;
     int hist_count = 0;
+    // Greedy decoder runs: the head GEMM's epilogue folds each row's argmax into ws.best, and the
+    // selection reads that instead of scanning the logits.
+    bool head_argmax = false;
     unsigned fused_bar_base = 0;         // the fused step's barrier count on the device
     std::vector<bst::FusedLayer> fused_table;
 
@@ -921,7 +924,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     add(reinterpret_cast<void**>(&ws.done), sizeof(int));
     add(reinterpret_cast<void**>(&ws.err), sizeof(int));
     add(reinterpret_cast<void**>(&ws.bar), 2 * sizeof(unsigned));
-    add(reinterpret_cast<void**>(&ws.best), 8 * sizeof(unsigned long long));
+    add(reinterpret_cast<void**>(&ws.best), std::max(8, rows) * sizeof(unsigned long long));
     add(reinterpret_cast<void**>(&ws.fused_stats), 8 * 256 * 2 * sizeof(double));
     {
         // Split planes for the widest tensor-core operand this run can see.
@@ -1280,6 +1283,7 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = ws.seg_row;
+    lg.best = head_argmax ? ws.best : nullptr;
     return linear(ws.last, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head", &lnf);
 }
 
@@ -1460,6 +1464,7 @@ int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens
     lg.out = ws.logits;
     lg.ldo = V;
     lg.rowmap = rowmap;
+    lg.best = head_argmax ? ws.best : nullptr;
     return x_normalised ? linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head",
                                  nullptr, false, true)
                         : linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head", &lnf);
@@ -1616,7 +1621,8 @@ int Engine::enqueue_select(Mode mode, int rows, int steps, float temperature, in
     if (mode == Mode::kGreedy) {
         err = launch(bst::kSelectGreedy, rows * V * 4.0, 0, 1, [&] {
             return bst::launch_select_greedy(stream, ws.logits, rows, V, W, steps, ws.step, ws.done,
-                                             ws.tokens_out, ws.next, ws.window);
+                                             ws.tokens_out, ws.next, ws.window,
+                                             head_argmax ? ws.best : nullptr);
         });
     } else {
         err = launch(bst::kSelectSample, rows * V * 4.0, 0, 1, [&] {
@@ -1694,6 +1700,10 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     if (!err && transformer && mode == Mode::kGreedy) {
         fused = prepare_fused(rows);
         if (fused < 0) return BST_PANIC;
+    }
+    head_argmax = transformer && mode == Mode::kGreedy;
+    if (!err && head_argmax) {
+        err = cudaMemsetAsync(ws.best, 0, sizeof(unsigned long long) * std::max(8, rows), stream);
     }
     if (!err && mode == Mode::kSample) {
         std::vector<uint64_t> states(rows);

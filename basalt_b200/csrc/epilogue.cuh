@@ -31,6 +31,21 @@ __device__ __forceinline__ void store_split(float v, int planes, void* hi, void*
     }
 }
 
+// Orders floats as unsigned integers (ascending), +0 and -0 equal; the low word prefers the
+// smaller index, so the largest packed value over a row is TextEngine.argmax's first maximum
+// (TextEngine.java:392-400). NaN scores are never packed: the reference never moves past index 0
+// to a NaN, and a NaN at index 0 is handled by whoever reads the result.
+__device__ __forceinline__ unsigned long long pack_best(float v, int idx) {
+    if (v == 0.0f) v = 0.0f;
+    const unsigned b = __float_as_uint(v);
+    const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(ord) << 32) | (0xffffffffu - static_cast<unsigned>(idx));
+}
+
+__device__ __forceinline__ int unpack_best_index(unsigned long long b) {
+    return static_cast<int>(0xffffffffu - static_cast<unsigned>(b));
+}
+
 template <Epi E>
 __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float v) {
     if constexpr (E == Epi::kStore) {
@@ -70,6 +85,7 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& ea, int m, int n, float
         }
     } else if constexpr (E == Epi::kLogits) {
         ea.out[static_cast<size_t>(ea.rowmap[m]) * ea.ldo + n] = v;
+        if (ea.best && !isnan(v)) atomicMax(ea.best + ea.rowmap[m], pack_best(v, n));
     }
 }
 

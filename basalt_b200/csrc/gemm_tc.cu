@@ -355,6 +355,18 @@ __device__ __forceinline__ void epilogue_row(const EpiArgs& ea, int m, int n, fl
         }
     } else if constexpr (E == Epi::kLogits) {
         store_row<CW>(ea.out + static_cast<size_t>(row_map) * ea.ldo + n, v, true);
+        if (ea.best) {
+            // One atomic per row chunk: the chunk's first maximum, packed.
+            unsigned long long b = 0ull;
+#pragma unroll
+            for (int j = 0; j < CW; ++j) {
+                if (!isnan(v[j])) {
+                    const unsigned long long p = pack_best(v[j], n + j);
+                    b = p > b ? p : b;
+                }
+            }
+            if (b) atomicMax(ea.best + row_map, b);
+        }
     }
 }
 
@@ -757,20 +769,43 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int 
     const float b = bias && n < N ? bias[n] : 0.0f;  // a weight: read before the wait
     pdl_trigger();
     pdl_wait();
-    if (n >= N) return;
+    // The logits epilogue folds the row's argmax: a warp's packed maximum, one atomic per warp, so
+    // every lane stays in the loop (lanes past N contribute nothing).
+    if (E != Epi::kLogits || ea.best == nullptr) {
+        if (n >= N) return;
+    }
     for (int m = blockIdx.y; m < M; m += gridDim.y) {
         const size_t e = static_cast<size_t>(m) * N + n;
-        // Up to 8 splits' loads in flight, then summed in split order.
-        float t[8];
-#pragma unroll
-        for (int z = 0; z < 8; ++z) t[z] = z < splits ? part[static_cast<size_t>(z) * total + e] : 0.0f;
         float v = 0.0f;
+        if (n < N) {
+            // Up to 8 splits' loads in flight, then summed in split order.
+            float t[8];
 #pragma unroll
-        for (int z = 0; z < 8; ++z) {
-            if (z < splits) v += t[z];
+            for (int z = 0; z < 8; ++z) t[z] = z < splits ? part[static_cast<size_t>(z) * total + e] : 0.0f;
+#pragma unroll
+            for (int z = 0; z < 8; ++z) {
+                if (z < splits) v += t[z];
+            }
+            for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
+            if (bias) v = __fadd_rn(v, b);
         }
-        for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
-        epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, b) : v);
+        if constexpr (E == Epi::kLogits) {
+            if (ea.best) {
+                unsigned long long p = 0ull;
+                if (n < N) {
+                    ea.out[static_cast<size_t>(ea.rowmap[m]) * ea.ldo + n] = v;
+                    if (!isnan(v)) p = pack_best(v, n);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long q = __shfl_xor_sync(0xffffffffu, p, o);
+                    p = q > p ? q : p;
+                }
+                if ((threadIdx.x & 31) == 0 && p) atomicMax(ea.best + ea.rowmap[m], p);
+                continue;
+            }
+        }
+        epi_apply<E>(ea, m, n, v);
     }
 }
 

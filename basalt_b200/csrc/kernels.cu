@@ -971,6 +971,28 @@ __global__ __launch_bounds__(256) void k_select_greedy(const float* __restrict__
     finish_row(r, token, s_step, rows, W, steps, step, done, tokens, next, window);
 }
 
+// Greedy selection when the head's epilogue already folded each row's first maximum into best[r]
+// (pack_best): the logits are not read again, except the row's score at index 0, which wins when
+// it is NaN (TextEngine.argmax only moves on to a larger score). best[r] is cleared for the next
+// step.
+__global__ __launch_bounds__(256) void k_select_greedy_packed(
+    const float* __restrict__ logits, unsigned long long* __restrict__ best, int V, int W,
+    int steps, int rows, int* step, int* done, int* tokens, int* next, int* window) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x;
+    __shared__ int s_step, s_token;
+    if (threadIdx.x == 0) {
+        s_step = *reinterpret_cast<volatile int*>(step);
+        const unsigned long long b = best[r];
+        best[r] = 0ull;
+        const float first = __ldcg(logits + static_cast<size_t>(r) * V);
+        s_token = (isnan(first) || b == 0ull) ? 0 : unpack_best_index(b);
+    }
+    __syncthreads();
+    finish_row(r, s_token, s_step, rows, W, steps, step, done, tokens, next, window);
+}
+
 // java.util.Random step and nextDouble (JDK specification).
 __device__ __forceinline__ int rng_next(uint64_t& s, int bits) {
     s = (s * 0x5DEECE66DULL + 0xBULL) & ((1ULL << 48) - 1);
@@ -1334,9 +1356,13 @@ cudaError_t launch_last_token(cudaStream_t s, const int* window, int W, const fl
 
 cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, int V, int W,
                                  int steps, int* step, int* done, int* tokens, int* next,
-                                 int* window) {
+                                 int* window, unsigned long long* best) {
     if (rows <= 0) return cudaSuccess;
     if (W > 8 * 256) return cudaErrorInvalidValue;
+    if (best) {
+        return launch_pdl(k_select_greedy_packed, rows, 256, 0, s, logits, best, V, W, steps, rows,
+                          step, done, tokens, next, window);
+    }
     return launch_pdl(k_select_greedy, rows, 256, 0, s, logits, V, W, steps, rows, step, done, tokens, next,
                                          window);
 }

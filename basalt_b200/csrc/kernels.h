@@ -64,6 +64,9 @@ struct EpiArgs {
     int d = 0, heads = 0, head_dim = 0, slots = 0;
     int kv_bf16 = 0;
     PlaneOut split;                // kStore, kGelu: also write the result as operand planes
+    // kLogits: per destination row, the packed first maximum of the row's logits (pack_best),
+    // combined with 64-bit atomicMax; nullptr when the caller selects from the logits itself.
+    unsigned long long* best = nullptr;
 };
 
 // Optional LayerNorm applied to a projection's input rows (the pre-norm of TransformerBlock).
@@ -146,10 +149,11 @@ cudaError_t launch_last_token(cudaStream_t s, const int* window, int W, const fl
 
 // Token selection plus the step bookkeeping shared by both modes: tokens[r*steps + step] = t,
 // next[r] = t, window[r] shifted left and t appended, and the device step counter advanced once
-// every row is done.
+// every row is done. With `best`, the head's epilogue folded each row's first maximum into
+// best[r] (EpiArgs::best) and the logits are not scanned again.
 cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, int V, int W,
                                  int steps, int* step, int* done, int* tokens, int* next,
-                                 int* window);
+                                 int* window, unsigned long long* best = nullptr);
 // TextEngine.draw (TextEngine.java:403-427) per row with java.util.Random state rng[r].
 cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, int V, int W,
                                  int steps, float temperature, int top_k, uint64_t* rng,

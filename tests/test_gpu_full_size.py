@@ -144,7 +144,11 @@ def test_v8192_d768_l12_8192_sequences_sampled_every_draw(runtime, weights):
     _, agreement = check_rows(oracle, ctx, rows, tokens[rows], logits, report, "c5",
                               sampled=(w.temperature, w.k, states))
     report_line("v8192-d768-l12-n8192-sampled", report, agreement, rows=rows)
-    assert_clean(report, rows)
+    # With 8192 near-uniform weights (T = 1) the cumulative boundaries lie ~1e-4 of the total
+    # apart, so fp32 logit differences of ~1e-5 leave some draws undecided: every difference must
+    # be one of those (no mismatches), and they stay rare.
+    assert not report.mismatches, f"token mismatches: {report.mismatches[:5]}"
+    assert agreement >= 0.95
     # A batch shard (the second half, as rank 1 of 2 decodes it) draws the same tokens.
     first = 4096
     engine.rng_state = shard_rng_state(w.sample_seed, w.steps, first)
