@@ -1685,6 +1685,10 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
         err = cudaMemcpyAsync(ws.hist_rows_of, hist_local.data(), sizeof(int) * hist_rows,
                               cudaMemcpyHostToDevice, stream);
     }
+    if (!err) err = cudaMemsetAsync(ws.step, 0, sizeof(int), stream);
+    if (!err) err = cudaMemsetAsync(ws.done, 0, sizeof(int), stream);
+    if (!err) err = cudaMemsetAsync(ws.err, 0, sizeof(int), stream);
+    if (!err) err = cudaMemsetAsync(ws.len, 0, sizeof(int) * rows, stream);
     // Host-side fault injection for tests of the failure path: the status word starts out set,
     // as a kernel that gave up on a bounded wait leaves it. No kernel is made to fail.
     int injected = 0;
@@ -1692,10 +1696,6 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     if (!err && injected) {
         err = cudaMemcpyAsync(ws.err, &injected, sizeof(int), cudaMemcpyHostToDevice, stream);
     }
-    if (!err) err = cudaMemsetAsync(ws.step, 0, sizeof(int), stream);
-    if (!err) err = cudaMemsetAsync(ws.done, 0, sizeof(int), stream);
-    if (!err) err = cudaMemsetAsync(ws.err, 0, sizeof(int), stream);
-    if (!err) err = cudaMemsetAsync(ws.len, 0, sizeof(int) * rows, stream);
     int fused = 0;
     if (!err && transformer && mode == Mode::kGreedy) {
         fused = prepare_fused(rows);

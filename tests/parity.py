@@ -112,6 +112,33 @@ def check_sampled_row(oracle, context, gpu_tokens, gpu_logits, temperature, top_
     return state
 
 
+def draw_undecided(scores: np.ndarray, temperature: float, top_k: int, state: int, delta: float):
+    """The tokens TextEngine.draw could return on `scores` moved by at most `delta` each.
+
+    A logit move of <= delta scales every weight exp((s - max) / T) by a factor within
+    exp(+-2 delta / T), so each cumulative boundary over the total moves by at most ~4 delta / T
+    (plus the double sums' rounding); and tokens whose scores lie within 2 delta of each other may
+    trade places in the sorted order. Returns the set of tokens whose buckets meet the target's
+    uncertainty interval, widened by those near-equal scores."""
+    scores = np.asarray(scores, dtype=np.float64)
+    order = np.lexsort((np.arange(scores.size), -scores))[:top_k]
+    t = np.float64(np.float32(temperature))
+    w = np.exp((scores[order] - scores[order[0]]) / t)
+    running = np.cumsum(w)
+    total = running[-1]
+    state = orc.lcg_advance(state, 1)
+    hi = state >> (48 - 26)
+    state = orc.lcg_advance(state, 1)
+    lo = state >> (48 - 27)
+    target = float(((hi << 27) + lo) * 2.0 ** -53) * total
+    eps = (4.0 * delta / t * 1.01 + DOUBLE_SUM_SLACK) * total
+    k0 = min(int(np.searchsorted(running, target - eps, side="left")), top_k - 1)
+    k1 = min(int(np.searchsorted(running, target + eps, side="left")), top_k - 1)
+    picked = scores[order[k0:k1 + 1]]
+    near = (scores[order] >= picked.min() - 2 * delta) & (scores[order] <= picked.max() + 2 * delta)
+    return set(int(x) for x in order[near])
+
+
 def check_rows(oracle, contexts, rows, gpu_tokens, gpu_logits, report: Report, where="",
                atol=ATOL, rtol=RTOL, sampled=None):
     """Teacher-forced comparison of several rows at once (oracle.forced_scores_rows).
@@ -133,16 +160,15 @@ def check_rows(oracle, contexts, rows, gpu_tokens, gpu_logits, report: Report, w
             if sampled:
                 # The GPU's draw replayed on its own logits must be exact (the sampler: sort order,
                 # double sums, target); against the oracle's logits a draw may differ only where
-                # the target sits closer to a cumulative boundary than the step's logit difference
-                # can move the boundaries: each weight exp((s - max) / T) moves by a factor within
-                # exp(+-2 delta / T), so running / total moves by at most ~4 delta / T.
+                # the step's logit difference leaves the draw undecided (draw_undecided).
                 own, _, _ = draw_margin(gpu_logits[i, step], sampled[0], sampled[1], state)
                 if own != int(token):
                     report.mismatches.append((here + " (sampler)", step, int(token), own))
-                want, margin, state = draw_margin(ref[i, step], sampled[0], sampled[1], state)
                 delta = float(np.max(np.abs(gpu_logits[i, step].astype(np.float64) -
                                             ref[i, step].astype(np.float64))))
-                near = margin < 4.0 * delta / sampled[0] * 1.01 + DOUBLE_SUM_SLACK
+                undecided = draw_undecided(ref[i, step], sampled[0], sampled[1], state, delta)
+                want, _, state = draw_margin(ref[i, step], sampled[0], sampled[1], state)
+                near = int(token) in undecided
             else:
                 want = int(np.argmax(ref[i, step]))
                 near = top2_gap(ref[i, step]) < atol
