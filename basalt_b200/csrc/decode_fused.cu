@@ -3,40 +3,37 @@
 // At batch 1 a decode step is ~60 small dependent operations (per layer: LayerNorm + QKV,
 // attention, output projection, LayerNorm + FFN1, FFN2; then the head and the argmax). Launched as
 // separate kernels each pays a launch, a ramp-up and a DRAM round trip with most SMs idle. Here a
-// single cooperative launch runs the whole step: one CTA per SM, 16 warps each. Every exchange of
-// a full activation vector between CTAs costs a grid barrier plus the global-memory round trips
-// around it, so the step is organised around as few of them as the data dependencies allow:
-// three grid barriers per layer.
+// single cooperative launch runs the whole step: one CTA per SM, 16 warps each, phases separated
+// by a grid barrier. Every projection spreads its weight rows over all SMs, so each weight byte is
+// read once per step with the whole chip's memory parallelism. Weights are constant during the
+// step: before the grid barrier that precedes a projection, each CTA has the TMA unit copy its
+// block of weight rows into shared memory (cp.async.bulk into this CTA only), so the weight stream
+// overlaps the barrier and the input staging.
 //
-//   A (attention block)  The CTAs are split into one group per head (cph = grid / heads CTAs
-//        each; leftover CTAs only wait). A group computes its head's q, k and v columns of the
-//        QKV projection (LN1 fused; k and v go straight into the cache at slot len), meets at a
-//        per-head counter, runs the head's attention over the cache (one warp per 32-key chunk;
-//        the last chunk of a (row, head) merges the chunk partials in chunk order and counts the
-//        head's merges), meets again, and multiplies the head's attention output by the head's
-//        block of the output projection: a partial output-projection vector per head.
-//   B    Every CTA sums the heads' partial vectors in head order, adds the bias and the residual
-//        (x' = x + O), layer-normalises x' itself (f64 statistics over the whole row, as
-//        nn_ops.rs:168-199) and computes its block of FFN1 columns with GELU.
-//   C    Every CTA computes its block of FFN2 columns, adds bias and residual to the residual
-//        columns it owns (kept in shared memory) and publishes LayerNorm partial statistics.
-//   head after the last layer: logits (final LN fused) and each CTA's first maximum, combined
-//        with a 64-bit atomic max; the last CTA to finish (ticket) applies TextEngine.argmax's
-//        rule, pushes the token into the window and advances the step counter and lengths.
-// (TransformerBlock.forward, torch/TransformerBlock.java:37-43, inside the padded decoder whose
-// last-position head follows TextEngine.scores, infer/TextEngine.java:96-112.)
+// Phases (R <= 8 rows, every row extending its cache; TransformerBlock.forward,
+// torch/TransformerBlock.java:37-43, inside the padded decoder whose last-position head follows
+// TextEngine.scores, infer/TextEngine.java:96-112):
+//   embed      every CTA computes x[i] = tok[next[i]] + pos[len[i]] itself (no barrier)
+//   per layer  QKV (LN1 fused; K/V stored at slot len[i]) | attention (one warp per 32-key
+//              chunk; the last chunk of a (row, head) merges the chunk partials in chunk order) |
+//              O + residual | FFN1 (LN2 fused) + GELU | FFN2 + residual
+//   head       logits (final LN fused) and each CTA's first maximum, combined with a 64-bit
+//              atomic max; the last CTA to finish (ticket) applies TextEngine.argmax's rule, pushes
+//              the token into the window and advances the step counter and lengths.
+// Each CTA owns the same block of residual columns of x in every phase and keeps it in shared
+// memory, so residual updates need no load.
 //
-// Weights are constant during the step, so each CTA has the TMA unit copy its share of the next
-// projections' weight rows into shared memory ahead of use, into one stage buffer per phase
-// (cp.async.bulk into this CTA only, mbarrier completion): the weight stream overlaps the
-// barriers and the activation loads. Rows that do not fit are read from global memory.
+// Code size matters as much as memory here: a phase runs for a few microseconds, too short to
+// amortise instruction fetches from L2. All projection phases therefore share one non-inlined
+// routine (the epilogue is chosen at run time) and attention is one routine per head size, so the
+// code a layer runs stays resident in the instruction cache. The row count is a template
+// parameter (1, or up to 8) so that batch 1 carries no code for other rows.
 //
-// Memory coherence: activations, the cache, partial sums and counters are written inside the
-// kernel by other CTAs, so they are read with ld.global.cg (L2) after an acquire, never through
+// Memory coherence: activations, the cache, scores and counters are written inside the kernel by
+// other CTAs, so they are read with ld.global.cg (L2) after the barrier's acquire, never through
 // the non-coherent read-only path; only weights and embeddings use that path. Every wait (grid
-// barrier, head-group counter, weight stage) is bounded by %globaltimer: on expiry it records an
-// error code in *err (11: grid barrier, 12: weight stage, 13: head-group counter) and the CTAs
-// return at the next grid barrier.
+// barrier, weight stage) is bounded by %globaltimer: on expiry it records an error code in *err
+// (11: grid barrier, 12: weight stage) and the CTAs return at the next barrier.
 
 #include <cuda_bf16.h>
 
@@ -54,10 +51,9 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxRows = 8;
 constexpr int kChunk = 32;
 constexpr int kMaxChunkGroups = 4;  // chunk merge handles up to 4 * 32 chunks (4096 keys)
-constexpr int kMaxHeadDim = 128;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any single wait
 constexpr size_t kSmemLimit = 212 * 1024;    // dynamic shared memory of one CTA
-constexpr int kOPrefetch = 1;                // output-projection weight vectors held per thread
+constexpr size_t kStageMax = 96 * 1024;      // weight stage
 
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -77,21 +73,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     return v;
 }
 
-// Waits (one thread) until *ctr has reached target; bounded. The caller syncs the block after.
-__device__ __forceinline__ void spin_until(const unsigned* ctr, unsigned target, int* err, int code,
-                                           int* abort_flag) {
-    if (static_cast<int>(ld_acquire(ctr) - target) >= 0) return;
-    const uint64_t start = global_ns();
-    while (static_cast<int>(ld_acquire(ctr) - target) < 0) {
-        if (*reinterpret_cast<volatile int*>(abort_flag)) return;
-        if (global_ns() - start > kWaitNs) {
-            atomicCAS(err, 0, code);
-            *abort_flag = 1;
-            return;
-        }
-    }
-}
-
 // Grid barrier over the co-resident CTAs of a cooperative launch: a counter that only grows.
 // Barrier b of a launch completes when the counter reaches base + b * gridDim.x, where the host
 // passes base (the count every earlier launch left behind). Returns false when this or an earlier
@@ -107,61 +88,53 @@ __device__ __forceinline__ bool grid_sync(GridSync& g) {
     __syncthreads();
     g.target += gridDim.x;
     if (threadIdx.x == 0) {
-        atom_add_acq_rel(g.count, 1);
-        spin_until(g.count, g.target, g.err, 11, g.abort_flag);
+        const unsigned old = atom_add_acq_rel(g.count, 1);
+        if (static_cast<int>(old + 1 - g.target) < 0) {
+            const uint64_t start = global_ns();
+            while (static_cast<int>(ld_acquire(g.count) - g.target) < 0) {
+                if (global_ns() - start > kWaitNs) {
+                    atomicCAS(g.err, 0, 11);
+                    *g.abort_flag = 1;
+                    break;
+                }
+            }
+        }
     }
     __syncthreads();
     return *reinterpret_cast<volatile int*>(g.abort_flag) == 0;
 }
 
-// Block `part` of `parts` equal blocks of [0, N).
-__device__ __forceinline__ void block_of(int N, int parts, int part, int* c0, int* c1) {
-    const int cpc = (N + parts - 1) / parts;
-    *c0 = min(N, part * cpc);
+// This CTA's share of an [N, K] weight matrix in a projection phase: a block of whole rows.
+__device__ __forceinline__ void column_block(int N, int* c0, int* c1) {
+    const int cpc = (N + gridDim.x - 1) / gridDim.x;
+    *c0 = min(N, static_cast<int>(blockIdx.x) * cpc);
     *c1 = min(N, *c0 + cpc);
 }
 
-// This CTA's share of an [N, K] weight matrix in a grid-wide projection: a block of whole rows.
-__device__ __forceinline__ void column_block(int N, int* c0, int* c1) {
-    block_of(N, gridDim.x, blockIdx.x, c0, c1);
-}
-
-// Virtual columns of a projection to matrix rows: the identity, or (h >= 0) the q, k and v blocks
-// of head h inside the fused [3d] QKV projection (virtual column j -> block j / hd).
-struct ColMap {
-    int d = 0, hd = 1, h = -1;
-    __device__ __forceinline__ int operator()(int v) const {
-        if (h < 0) return v;
-        const int blk = v / hd;
-        return blk * d + h * hd + (v - blk * hd);
-    }
-};
-
-// How a CTA's threads cover its columns [c0, c1) of a projection with nvec 16-byte weight vectors
-// per column. Up to 16 columns: `ks` whole warps per column, each on a contiguous part of K. More
+// How a CTA's threads cover its columns of a projection with nvec 16-byte weight vectors per
+// column. Up to 16 columns: `ks` whole warps per column, each on a contiguous part of K. More
 // columns: groups of `gs` lanes (a power of two) per column, repeated `reps` times when there are
 // more columns than groups.
 struct Plan {
     int c0, c1;
     int gs, ks, reps;
-    int col;         // this thread's column in rep 0
+    int col;         // this thread's column in rep 0 (absolute)
     int col_stride;  // column step between reps
     int vbeg, vend, vstep;
     int part;        // warp's part of its column (gs == 32)
 };
 
-__device__ __forceinline__ Plan make_plan(int c0, int c1, int nvec) {
+__device__ __forceinline__ Plan make_plan(int N, int nvec) {
     Plan p;
-    p.c0 = c0;
-    p.c1 = c1;
-    const int ncols = c1 - c0;
+    column_block(N, &p.c0, &p.c1);
+    const int ncols = p.c1 - p.c0;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (ncols <= kWarps) {
         p.gs = 32;
         p.ks = ncols > 0 ? kWarps / ncols : 1;
         p.reps = 1;
         p.part = warp % p.ks;
-        p.col = c0 + warp / p.ks;
+        p.col = p.c0 + warp / p.ks;
         p.col_stride = 0;
         const int per = (nvec + p.ks - 1) / p.ks;
         p.vbeg = p.part * per + lane;
@@ -175,7 +148,7 @@ __device__ __forceinline__ Plan make_plan(int c0, int c1, int nvec) {
         p.ks = 1;
         p.part = 0;
         p.reps = (ncols + groups - 1) / groups;
-        p.col = c0 + tid / gs;
+        p.col = p.c0 + tid / gs;
         p.col_stride = groups;
         p.vbeg = tid % gs;
         p.vend = nvec;
@@ -241,83 +214,75 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
-// A weight stage: a shared-memory buffer the TMA unit fills with this CTA's rows of one
-// projection (as many whole rows as fit; the rest is read from global memory) plus the
-// LayerNorm parameters of the projection's input. The descriptor lives in shared memory and only
-// thread 0 changes it; every thread reads it after a __syncthreads().
+// The CTA's weight stage: a shared-memory buffer the TMA unit fills with the CTA's block of the
+// next projection's weight rows (as many whole rows as fit; the rest is read from global memory),
+// plus the bias of those rows and the LayerNorm parameters of the projection's input.
 struct WStage {
-    uint64_t bar;           // mbarrier, one phase per issued copy
-    unsigned char* buf;     // weight rows (shared), in virtual column order
-    float* lnp;             // gamma [K], beta [K] (shared), or nullptr
+    uint64_t* bar;          // mbarrier (shared), one phase per issued copy
+    unsigned char* buf;     // weight rows (shared)
     unsigned cap;           // bytes
+    float* bias;            // [columns + 4] (shared), column c0 + j at bias[j + bias_off]
+    float* lnp;             // gamma [K], beta [K] (shared)
+    int* abort_flag;        // shared
+    int* err;
     unsigned parity;        // phase the next wait expects
     int cols;               // weight rows of the current projection held in buf
-    int pending;            // a copy was issued and not yet waited for
+    int bias_off;           // bias block starts bias_off floats before column c0
+    bool pending;           // a copy was issued and not yet waited for
 };
 
-// Issues the stage of virtual columns [c0, c1) of Y[R, N] = X W^T (W [N, K] of WT) for this CTA.
-// Every thread of the CTA calls it; thread 0 records it and issues the copies.
+// Issues the stage of the projection Y[R, N] = X W^T (W [N, K] of WT) for this CTA.
 template <typename WT>
-__device__ __forceinline__ void stage_issue(const void* w, int K, int c0, int c1, ColMap cm,
-                                            const float* ln_gamma, const float* ln_beta,
-                                            WStage& st) {
-    if (c1 <= c0) return;  // uniform over the CTA
+__device__ __forceinline__ void stage_issue(const void* w, const float* bias, int N, int K,
+                                         const float* ln_gamma, const float* ln_beta, WStage& st) {
+    int c0, c1;
+    column_block(N, &c0, &c1);
     const size_t row_bytes = static_cast<size_t>(K) * sizeof(WT);
-    // Every thread is done with this buffer's previous contents: hand it to the TMA unit.
+    st.cols = c1 > c0 ? min(c1 - c0, static_cast<int>(st.cap / row_bytes)) : 0;
+    st.bias_off = c0 & 3;
+    st.pending = c1 > c0;
+    if (c1 <= c0) return;  // uniform over the CTA
+    // Every thread is done with the previous projection's stage: hand it to the TMA unit. All of
+    // it arrives by bulk copies on one mbarrier: the weight rows, the LayerNorm parameters and the
+    // bias block (its start rounded down, its end up, to 16 bytes).
     __syncthreads();
     if (threadIdx.x == 0) {
-        const int cols = min(c1 - c0, static_cast<int>(st.cap / row_bytes));
-        st.cols = cols;
-        st.pending = 1;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const uint32_t lbytes = ln_gamma && st.lnp ? static_cast<uint32_t>(K) * 4u : 0u;
-        mbar_expect_tx(&st.bar, static_cast<uint32_t>(cols * row_bytes) + 2 * lbytes);
-        // Runs of virtual columns that are contiguous matrix rows: one copy each.
-        int v = c0;
-        while (v < c0 + cols) {
-            const int row0 = cm(v);
-            int n = 1;
-            while (v + n < c0 + cols && cm(v + n) == row0 + n) ++n;
-            bulk_load(st.buf + static_cast<size_t>(v - c0) * row_bytes,
-                      static_cast<const WT*>(w) + static_cast<size_t>(row0) * K,
-                      static_cast<uint32_t>(n * row_bytes), &st.bar);
-            v += n;
+        const uint32_t wbytes = static_cast<uint32_t>(st.cols * row_bytes);
+        const uint32_t lbytes = ln_gamma ? static_cast<uint32_t>(K) * 4u : 0u;
+        const uint32_t bbytes = bias ? static_cast<uint32_t>((c1 - c0 + st.bias_off + 3) / 4 * 16) : 0u;
+        mbar_expect_tx(st.bar, wbytes + 2 * lbytes + bbytes);
+        if (wbytes) {
+            bulk_load(st.buf, static_cast<const WT*>(w) + static_cast<size_t>(c0) * K, wbytes, st.bar);
         }
         if (lbytes) {
-            bulk_load(st.lnp, ln_gamma, lbytes, &st.bar);
-            bulk_load(st.lnp + K, ln_beta, lbytes, &st.bar);
+            bulk_load(st.lnp, ln_gamma, lbytes, st.bar);
+            bulk_load(st.lnp + K, ln_beta, lbytes, st.bar);
         }
+        if (bbytes) bulk_load(st.bias, bias + (c0 - st.bias_off), bbytes, st.bar);
     }
 }
 
 // Waits for the stage issued by stage_issue (bounded; on expiry records code 12, waits once more
-// for the copy to land and lets the next grid barrier end the kernel). Every thread of the CTA
-// calls it; idempotent.
-__device__ __forceinline__ void stage_wait(WStage& st, int* err, int* abort_flag) {
-    __syncthreads();
-    if (!st.pending) return;  // uniform: read after the barrier, changed only below
-    const unsigned parity = st.parity;
-    if (!mbar_try_wait(&st.bar, parity)) {
-        uint64_t start = global_ns();
-        bool late = false;
-        while (!mbar_try_wait(&st.bar, parity)) {
-            if (global_ns() - start > kWaitNs) {
-                if (late) break;
-                if (threadIdx.x == 0) {
-                    atomicCAS(err, 0, 12);
-                    *abort_flag = 1;
+// for the copy to land and lets the next grid barrier end the kernel).
+__device__ __forceinline__ void stage_wait(WStage& st) {
+    if (st.pending) {
+        if (!mbar_try_wait(st.bar, st.parity)) {
+            uint64_t start = global_ns();
+            bool late = false;
+            while (!mbar_try_wait(st.bar, st.parity)) {
+                if (global_ns() - start > kWaitNs) {
+                    if (late) break;
+                    atomicCAS(st.err, 0, 12);
+                    *st.abort_flag = 1;
+                    late = true;
+                    start = global_ns();
                 }
-                late = true;
-                start = global_ns();
             }
         }
+        st.parity ^= 1u;
+        st.pending = false;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        st.parity = parity ^ 1u;
-        st.pending = 0;
-    }
-    __syncthreads();
 }
 
 // Copies rows [R][K] (row stride ldx, K % 4 == 0) from global memory into shared memory.
@@ -339,8 +304,7 @@ struct Sink {
     unsigned long long* best = nullptr;  // kLogits: per-row packed maximum (shared)
 };
 
-// One output of a projection through its epilogue (chosen at run time). c0: the CTA's first
-// residual column (kResidual).
+// One output of a projection through its epilogue (chosen at run time).
 __device__ __forceinline__ void store_out(Epi epi, const EpiArgs& ea, const Sink& sk, int c0, int m,
                                        int n, float v) {
     switch (epi) {
@@ -432,57 +396,66 @@ __device__ __forceinline__ void combine_stats(const double* stats, int R, int d,
     }
 }
 
-// xs = LayerNorm(xraw) for R rows of width K, from the published statistics (stats != nullptr) or
-// from the rows themselves, with gamma/beta in lnp [2][K] (shared). Ends with __syncthreads().
-template <int RT>
-__device__ __forceinline__ void normalise_rows(const float* xraw, int R, int K, const double* stats,
-                                               float eps, const float* lnp, float* xs) {
-    __shared__ double s_mean[RT], s_inv[RT];
-    if (stats) {
-        combine_stats(stats, R, K, eps, s_mean, s_inv);
+// Per-CTA state shared by the projection phases.
+struct Ctx {
+    float* xs;    // [R][max(d, F)] projection input (shared)
+    float* xraw;  // [R][d] rows before LayerNorm (shared)
+    int R;
+    float eps;
+    const double* stats;  // published per-CTA statistics of the input rows (LayerNorm phases)
+};
+
+// Y[R, N] = X[R, K] * W[N, K]^T + bias over the whole grid with the weights staged by
+// stage_issue. The input rows are staged in shared memory (already in xraw when `staged`),
+// layer-normalised first when `ln`. Partial sums are combined in a fixed order, so results repeat
+// bit for bit.
+template <typename WT, int RT>
+__device__ __forceinline__ void gemv(const float* x, int ldx, bool staged, bool ln, bool use_stats,
+                                  const void* wv, bool has_bias, int N, int K, Epi epi,
+                                  const EpiArgs& ea, const Sink& sk, const Ctx& cx, WStage& st) {
+    constexpr int VEC = Unpack<WT>::N;
+    __shared__ float red[kWarps][RT];
+    const int R = cx.R;
+    float* xs = cx.xs;
+    const int nvec = K / VEC;
+    const Plan pl = make_plan(N, nvec);
+    if (pl.c1 <= pl.c0) return;  // uniform over the CTA
+    if (ln && use_stats) {
+        __shared__ double s_mean[RT], s_inv[RT];
+        stage_rows(x, ldx, R, K, cx.xraw);
+        combine_stats(cx.stats, R, K, cx.eps, s_mean, s_inv);
+        stage_wait(st);
         __syncthreads();
         for (int e = threadIdx.x; e < R * K; e += kThreads) {
             const int i = e / K, k = e - i * K;
             const float nrm = static_cast<float>(
-                __dmul_rn(__dadd_rn(static_cast<double>(xraw[e]), -s_mean[i]), s_inv[i]));
-            xs[e] = __fadd_rn(__fmul_rn(nrm, lnp[k]), lnp[K + k]);
+                __dmul_rn(__dadd_rn(static_cast<double>(cx.xraw[e]), -s_mean[i]), s_inv[i]));
+            xs[e] = __fadd_rn(__fmul_rn(nrm, st.lnp[k]), st.lnp[K + k]);
         }
+    } else if (ln) {
+        if (!staged) stage_rows(x, ldx, R, K, cx.xraw);
+        stage_wait(st);
+        __syncthreads();
+        const LnArgs lns{st.lnp, st.lnp + K, cx.eps};
+        layernorm_rows(cx.xraw, K, RT == 1 ? 1 : R, K, lns, xs);
     } else {
-        const LnArgs lns{lnp, lnp + K, eps};
-        layernorm_rows(xraw, K, RT == 1 ? 1 : R, K, lns, xs);
+        stage_rows(x, ldx, R, K, xs);
+        stage_wait(st);
     }
     __syncthreads();
-}
-
-// Y[R, columns c0..c1) = X[R, K] * W[cm(c), K]^T + bias[cm(c)] with the inputs already in xs
-// (shared, [R][K]) and the weight rows staged by stage_issue. Partial sums are combined in a fixed
-// order, so results repeat bit for bit.
-template <typename WT, int RT>
-__device__ __forceinline__ void gemv(const float* xs, int R, int K, int c0, int c1, ColMap cm,
-                                     const void* wv, const float* bias, Epi epi, const EpiArgs& ea,
-                                     const Sink& sk, int res_c0, WStage& st, int* err,
-                                     int* abort_flag) {
-    constexpr int VEC = Unpack<WT>::N;
-    __shared__ float red[kWarps][RT];
-    const int nvec = K / VEC;
-    const Plan pl = make_plan(c0, c1, nvec);
-    if (c1 <= c0) return;  // uniform over the CTA
-    stage_wait(st, err, abort_flag);
     const WT* w = static_cast<const WT*>(wv);
     const uint4* staged_w = reinterpret_cast<const uint4*>(st.buf);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int rep = 0; rep < pl.reps; ++rep) {
         const int col = pl.col + rep * pl.col_stride;
         const bool act = col < pl.c1;
-        const int mcol = act ? cm(col) : 0;
-        const float b = act && bias ? __ldg(bias + mcol) : 0.0f;
         float acc[RT];
 #pragma unroll
         for (int i = 0; i < RT; ++i) acc[i] = 0.0f;
         if (act) {
             const bool in_smem = col - pl.c0 < st.cols;
             const uint4* wc = in_smem ? staged_w + static_cast<size_t>(col - pl.c0) * nvec
-                                      : reinterpret_cast<const uint4*>(w + static_cast<size_t>(mcol) * K);
+                                      : reinterpret_cast<const uint4*>(w + static_cast<size_t>(col) * K);
 #pragma unroll 2
             for (int v = pl.vbeg; v < pl.vend; v += pl.vstep) {
                 float wf[VEC];
@@ -526,9 +499,10 @@ __device__ __forceinline__ void gemv(const float* xs, int R, int K, int c0, int 
             storer = act && threadIdx.x % pl.gs == 0;
         }
         if (storer) {
+            const float b = has_bias ? st.bias[col - pl.c0 + st.bias_off] : 0.0f;
 #pragma unroll
             for (int i = 0; i < RT; ++i) {
-                if (i < R) store_out(epi, ea, sk, res_c0, i, mcol, bias ? __fadd_rn(acc[i], b) : acc[i]);
+                if (i < R) store_out(epi, ea, sk, pl.c0, i, col, has_bias ? __fadd_rn(acc[i], b) : acc[i]);
             }
         }
     }
@@ -541,17 +515,14 @@ __device__ __forceinline__ void load_cg16(const KT* p, float* o) {
     Unpack<KT>::run(u, o);
 }
 
-// Decode attention of head h over every (row, 32-key chunk) that holds keys, by `workers` warps
-// (this one is number `worker`): one warp per chunk. Lanes own keys for the scores; for P.V lanes
-// own (key group, 16-byte slice of the head) pairs so that every V load of the chunk is
-// independent. The last chunk of a (row, head) to finish (ticket) merges the chunk partials in
-// chunk order, writes the row's attention output for the head and counts one merge on `merged`.
+// Decode attention over every (row, head, 32-key chunk) that holds keys: one warp per chunk. Lanes
+// own keys for the scores; for P.V lanes own (key group, 16-byte slice of the head) pairs so that
+// every V load of the chunk is independent. The last chunk of a (row, head) to finish (ticket)
+// merges the chunk partials in chunk order, lanes in parallel over chunks and dimensions.
 template <typename KT, int HD>
-__device__ __forceinline__ void attention_head(int h, int worker, int workers, const float* q,
-                                               const KT* kc, const KT* vc, const int* s_len, int R,
-                                               int heads, int slots, int nchunks, float scale,
-                                               float* part, int* tickets, float* out,
-                                               unsigned* merged, float* qslot) {
+__device__ __forceinline__ void attention_phase(const float* q, const KT* kc, const KT* vc, const int* s_len,
+                                int R, int heads, int slots, int nchunks, float scale, float* part,
+                                int* tickets, float* out, float* qslot) {
     constexpr int VE = 16 / sizeof(KT);  // elements per 16-byte vector
     constexpr int DV = HD / VE;          // vectors per key row
     constexpr int KG = 32 / DV;          // key groups for P.V (>= 1)
@@ -563,10 +534,12 @@ __device__ __forceinline__ void attention_head(int h, int worker, int workers, c
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = heads * HD;
     float* qw = qslot + warp * HD;
-    const int tasks = R * nchunks;
-    for (int task = worker; task < tasks; task += workers) {
-        const int i = task / nchunks;
-        const int c = task - i * nchunks;
+    const int tasks = R * heads * nchunks;
+    // Task t runs on CTA t % grid: consecutive chunks land on different SMs.
+    for (int task = warp * gridDim.x + blockIdx.x; task < tasks; task += gridDim.x * kWarps) {
+        const int i = task / (heads * nchunks);
+        const int rem = task - i * heads * nchunks;
+        const int h = rem / nchunks, c = rem - h * nchunks;
         const int T = s_len[i] + 1;  // cached keys plus this step's
         const int nck = (T + kChunk - 1) / kChunk;
         if (c >= nck) continue;
@@ -702,124 +675,84 @@ __device__ __forceinline__ void attention_head(int h, int worker, int workers, c
                 out[static_cast<size_t>(i) * d + h * HD + lane * DPL + cc] = __fdiv_rn(O[cc], L);
             }
             if (lane == 0) tickets[i * heads + h] = 0;
-            // Count the merge: a release of the output written above (ordered by __syncwarp).
-            __syncwarp();
-            if (lane == 0) atom_add_acq_rel(merged, 1);
         }
         __syncwarp();
     }
 }
 
 template <typename KT>
-__device__ __forceinline__ void attention(int hd, int h, int worker, int workers, const float* q,
-                                          const void* kc, const void* vc, const int* s_len, int R,
-                                          int heads, int slots, int nchunks, float scale,
-                                          float* part, int* tickets, float* out, unsigned* merged,
-                                          float* qslot) {
+__device__ __forceinline__ void attention(int hd, const float* q, const void* kc, const void* vc,
+                                          const int* s_len, int R, int heads, int slots,
+                                          int nchunks, float scale, float* part, int* tickets,
+                                          float* out, float* qslot) {
     const KT* k = static_cast<const KT*>(kc);
     const KT* v = static_cast<const KT*>(vc);
     if (hd == 32) {
-        attention_head<KT, 32>(h, worker, workers, q, k, v, s_len, R, heads, slots, nchunks, scale,
-                               part, tickets, out, merged, qslot);
+        attention_phase<KT, 32>(q, k, v, s_len, R, heads, slots, nchunks, scale, part, tickets, out, qslot);
     } else if (hd == 64) {
-        attention_head<KT, 64>(h, worker, workers, q, k, v, s_len, R, heads, slots, nchunks, scale,
-                               part, tickets, out, merged, qslot);
+        attention_phase<KT, 64>(q, k, v, s_len, R, heads, slots, nchunks, scale, part, tickets, out, qslot);
     } else {
-        attention_head<KT, 128>(h, worker, workers, q, k, v, s_len, R, heads, slots, nchunks, scale,
-                                part, tickets, out, merged, qslot);
+        attention_phase<KT, 128>(q, k, v, s_len, R, heads, slots, nchunks, scale, part, tickets, out, qslot);
     }
 }
 
-// The head's block of the output projection for this CTA's columns [c0, c1) of d:
-// opart[i][n] = sum_e att[i][e] * Wo[n][h * hd + e], with the weight vectors (16 bytes each, vpc
-// per column) of the first round preloaded in `pre`.
-template <typename WT, int RT>
-__device__ __forceinline__ void head_output_block(const float* att, int R, int hd, int h, int d,
-                                                  int c0, int c1, const WT* wo, const uint4* pre,
-                                                  float* opart) {
-    constexpr int VEC = Unpack<WT>::N;
-    const int vpc = hd / VEC;  // a power of two <= 32: whole lane groups of one warp
-    const int total = (c1 - c0) * vpc;
-    const int rounds = (total + kThreads - 1) / kThreads;
-#pragma unroll 1
-    for (int r = 0; r < rounds; ++r) {
-        const int e = r * kThreads + static_cast<int>(threadIdx.x);
-        const bool act = e < total;
-        const int col = c0 + (act ? e / vpc : 0), v = act ? e % vpc : 0;
-        uint4 u = make_uint4(0, 0, 0, 0);
-        if (act) {
-            u = r == 0 ? pre[0]
-                       : __ldg(reinterpret_cast<const uint4*>(wo + static_cast<size_t>(col) * d + h * hd) + v);
-        }
-        float wf[VEC];
-        Unpack<WT>::run(u, wf);
-        float acc[RT];
-#pragma unroll
-        for (int i = 0; i < RT; ++i) {
-            acc[i] = 0.0f;
-            if (act && i < R) {
-#pragma unroll
-                for (int c = 0; c < VEC; ++c) acc[i] = fmaf(wf[c], att[i * hd + v * VEC + c], acc[i]);
-            }
-        }
-        for (int o = vpc >> 1; o > 0; o >>= 1) {
-#pragma unroll
-            for (int i = 0; i < RT; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
-        }
-        if (act && v == 0) {
-#pragma unroll
-            for (int i = 0; i < RT; ++i) {
-                if (i < R) opart[static_cast<size_t>(i) * d + col] = acc[i];
-            }
-        }
+// Operands of one projection phase. Phase p < 5L is kind p % 5 of layer p / 5 (0 QKV, 1 attention,
+// 2 output projection, 3 FFN1, 4 FFN2); phase 5L is the head.
+struct ProjDesc {
+    const void* w;
+    const float* bias;
+    const float* ln_g;  // input LayerNorm (nullptr: none)
+    const float* ln_b;
+    const float* x;     // input rows
+    int ldx, N, K;
+    Epi epi;
+};
+
+__device__ __forceinline__ ProjDesc describe(const FusedStep& p, const FusedLayer* lt, int phase) {
+    ProjDesc pd;
+    const int d = p.d;
+    if (phase >= 5 * p.L) {
+        pd = ProjDesc{p.head_w, p.head_b, p.lnf_g, p.lnf_b, p.x, d, p.V, d, Epi::kLogits};
+        return pd;
     }
+    const FusedLayer& lw = lt[phase / 5];
+    switch (phase % 5) {
+        case 0: pd = ProjDesc{lw.wqkv, lw.bqkv, lw.ln1_g, lw.ln1_b, p.x, d, 3 * d, d, Epi::kQkv}; break;
+        case 2: pd = ProjDesc{lw.wo, lw.bo, nullptr, nullptr, p.att, d, d, d, Epi::kResidual}; break;
+        case 3: pd = ProjDesc{lw.w1, lw.b1, lw.ln2_g, lw.ln2_b, p.x, d, p.F, d, Epi::kGelu}; break;
+        case 4: pd = ProjDesc{lw.w2, lw.b2, nullptr, nullptr, p.ffn, p.F, d, p.F, Epi::kResidual}; break;
+        default: pd = ProjDesc{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0, Epi::kStore}; break;
+    }
+    return pd;
 }
 
 template <typename WT, typename KT, int RT>
 __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
                                                              const FusedLayer* __restrict__ layers) {
-    // After a timed-out wait in an earlier step of the run, the barrier and head counters no
-    // longer match what this launch expects: return at once (the host reports the error recorded
-    // in *err once the run's queued steps have drained).
-    if (__ldcg(p.err) != 0) return;
     extern __shared__ __align__(16) float smem[];
-    __shared__ __align__(16) float qslot[kWarps * kMaxHeadDim];
-    __shared__ __align__(16) float s_att[kMaxRows * kMaxHeadDim];
+    __shared__ __align__(16) float qslot[kWarps * 128];
     __shared__ int abort_flag, s_len[kMaxRows], s_next[kMaxRows], s_rows[kMaxRows], s_step, s_last;
     __shared__ unsigned long long s_best[kMaxRows];
-    __shared__ __align__(16) WStage s_stage[3];  // A: QKV slice / head, B: FFN1, C: FFN2
-    const int R = p.R, d = p.d, F = p.F, H = p.H, L = p.L;
-    const int hd = d / H;
-    const int G = gridDim.x;
-    const int cph = G / H;  // CTAs per head group
-    const int grp = static_cast<int>(blockIdx.x) < cph * H ? static_cast<int>(blockIdx.x) / cph : -1;
-    const int mem = static_cast<int>(blockIdx.x) % cph;
-    const int own_ld = (d + G - 1) / G;
-    const int widest = max(d, F);
-    float* xs = smem;                                   // [R][max(d, F)] projection input
-    float* xraw = xs + static_cast<size_t>(R) * widest;  // [R][d] residual stream x
-    float* xprime = xraw + static_cast<size_t>(R) * d;  // [R][d] x + attention output
-    float* lnA = xprime + static_cast<size_t>(R) * d;   // LayerNorm gamma, beta [2][d] (stage A)
-    float* lnB = lnA + 2 * static_cast<size_t>(d);      // (stage B)
-    float* xown = lnB + 2 * static_cast<size_t>(d);     // [R][own_ld]
+    __shared__ __align__(8) uint64_t s_wbar;
+    // After a timed-out barrier or weight stage in an earlier step of the run, the barrier count
+    // no longer matches what this launch expects: return at once (the host reports the error
+    // recorded in *err once the run's queued steps have drained).
+    if (__ldcg(p.err) != 0) return;
+    const int R = p.R, d = p.d, F = p.F;
+    int dc0, dc1;
+    column_block(d, &dc0, &dc1);
+    const int own_ld = (d + gridDim.x - 1) / gridDim.x;
+    float* xs = smem;                                        // [R][max(d, F)]
+    float* xraw = xs + static_cast<size_t>(R) * max(d, F);   // [R][d]
+    float* lnp = xraw + static_cast<size_t>(R) * d;          // LayerNorm gamma, beta [2][d]
+    float* xown = lnp + 2 * static_cast<size_t>(d);          // [R][own_ld]
+    float* bsm = xown + ((R * own_ld + 3) & ~3);             // [bias_cap], 16-byte aligned
     FusedLayer* lt = reinterpret_cast<FusedLayer*>(reinterpret_cast<unsigned char*>(smem) + p.table_offset);
+    unsigned char* wbuf = reinterpret_cast<unsigned char*>(smem) + p.wstage_offset;
     if (threadIdx.x == 0) {
         abort_flag = 0;
         s_step = __ldcg(p.step);
-        unsigned char* base = reinterpret_cast<unsigned char*>(smem) + p.wstage_offset;
-        const unsigned caps[3] = {p.wstage_a, p.wstage_b, p.wstage_c};
-        float* lnps[3] = {lnA, lnB, nullptr};
-        for (int b = 0; b < 3; ++b) {
-            WStage& st = s_stage[b];
-            st.buf = base;
-            base += caps[b];
-            st.lnp = lnps[b];
-            st.cap = caps[b];
-            st.parity = 0;
-            st.cols = 0;
-            st.pending = 0;
-            mbar_init(&st.bar, 1);
-        }
+        mbar_init(&s_wbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x < R) {
@@ -832,38 +765,30 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
     {
         const unsigned long long* src = reinterpret_cast<const unsigned long long*>(layers);
         unsigned long long* dst = reinterpret_cast<unsigned long long*>(lt);
-        const int words = L * static_cast<int>(sizeof(FusedLayer) / 8);
+        const int words = p.L * static_cast<int>(sizeof(FusedLayer) / 8);
         for (int i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
     }
     GridSync gsync{p.bar, p.bar_base, p.err, &abort_flag};
+    WStage st{&s_wbar, wbuf, p.wstage_bytes, bsm, lnp, &abort_flag, p.err, 0u, 0, 0, false};
+    const Ctx cx{xs, xraw, R, p.eps, p.stats};
     __syncthreads();
-
-    // Column blocks (kept in shared memory, read at phase boundaries): this CTA's QKV slice of its
-    // head (virtual columns of the head's 3 * hd), its output-projection columns within the head
-    // group, and its blocks of the grid-wide projections.
-    enum { kQ0, kQ1, kO0, kO1, kF0, kF1, kD0, kD1, kV0, kV1 };
-    __shared__ int cb[10];
-    if (threadIdx.x == 0) {
-        cb[kQ0] = cb[kQ1] = cb[kO0] = cb[kO1] = 0;
-        if (grp >= 0) {
-            block_of(3 * hd, cph, mem, &cb[kQ0], &cb[kQ1]);
-            block_of(d, cph, mem, &cb[kO0], &cb[kO1]);
-        }
-        column_block(F, &cb[kF0], &cb[kF1]);
-        column_block(d, &cb[kD0], &cb[kD1]);
-        column_block(p.V, &cb[kV0], &cb[kV1]);
+    {
+        const ProjDesc pd = describe(p, lt, 0);
+        stage_issue<WT>(pd.w, pd.bias, pd.N, pd.K, pd.ln_g, pd.ln_b, st);
     }
-    __syncthreads();
-    stage_issue<WT>(lt[0].wqkv, d, cb[kQ0], cb[kQ1], ColMap{d, hd, grp}, lt[0].ln1_g, lt[0].ln1_b,
-                    s_stage[0]);
 
-    // embed, in every CTA: the full rows into xraw
+    // embed, in every CTA: the full rows into xraw; the CTA's own columns into xown and x
     const WT* tok = static_cast<const WT*>(p.tok_emb);
     const WT* pos = static_cast<const WT*>(p.pos_emb);
     for (int e = threadIdx.x; e < R * d; e += kThreads) {
         const int i = e / d, k = e - i * d;
-        xraw[e] = __fadd_rn(to_f(tok[static_cast<size_t>(s_next[i]) * d + k]),
-                            to_f(pos[static_cast<size_t>(s_len[i]) * d + k]));
+        const float v = __fadd_rn(to_f(tok[static_cast<size_t>(s_next[i]) * d + k]),
+                                  to_f(pos[static_cast<size_t>(s_len[i]) * d + k]));
+        xraw[e] = v;
+        if (k >= dc0 && k < dc1) {
+            xown[i * own_ld + (k - dc0)] = v;
+            p.x[e] = v;
+        }
     }
 
     Sink sk;
@@ -873,149 +798,42 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
     sk.step = s_step;
     sk.steps = p.steps;
     sk.best = s_best;
-    // Head-group counters: [0, H) QKV arrivals (cph per layer), [H, 2H) merges (R per layer).
-    unsigned* head_arrive = p.head_ctr;
-    unsigned* head_merged = p.head_ctr + H;
-    const unsigned arrive_base = p.launch_index * static_cast<unsigned>(L * cph);
-    const unsigned merged_base = p.launch_index * static_cast<unsigned>(L * R);
-
-    // Phase ph of the step: kind ph % 3 of layer ph / 3 (0: A, 1: B, 2: C), then the head. Each
-    // phase has one LayerNorm site and one projection site, shared by all kinds.
-    const int last = 3 * L;
-    for (int ph = 0; ph <= last; ++ph) {
-        const int kind = ph < last ? ph % 3 : 3;
-        const int l = min(ph / 3, L - 1);
-        const FusedLayer& lw = lt[l];
-        // ---- before the projection ----
-        uint4 wpre[kOPrefetch];
-        if (kind == 0) {
-            stage_issue<WT>(lw.w1, d, cb[kF0], cb[kF1], ColMap{}, lw.ln2_g, lw.ln2_b, s_stage[1]);
-            if (l > 0) stage_rows(p.x, d, R, d, xraw);
-            // The output-projection weights of this CTA's block, loaded early (they are constant).
-            constexpr int VEC = Unpack<WT>::N;
-            const int vpc = hd / VEC;
-            const int total = grp >= 0 ? (cb[kO1] - cb[kO0]) * vpc : 0;
-#pragma unroll
-            for (int r = 0; r < kOPrefetch; ++r) {
-                const int e = r * kThreads + static_cast<int>(threadIdx.x);
-                wpre[r] = e < total ? __ldg(reinterpret_cast<const uint4*>(
-                                          static_cast<const WT*>(lw.wo) +
-                                          static_cast<size_t>(cb[kO0] + e / vpc) * d + grp * hd) + e % vpc)
-                                    : make_uint4(0, 0, 0, 0);
-            }
-        } else if (kind == 1) {
-            stage_issue<WT>(lw.w2, F, cb[kD0], cb[kD1], ColMap{}, nullptr, nullptr, s_stage[2]);
-            // x' = x + (sum over heads of the partial output projections, in head order) + bias
-            for (int e = threadIdx.x; e < R * d; e += kThreads) {
-                const int i = e / d, n = e - i * d;
-                float t[8];
-                float o = 0.0f;
-                for (int h0 = 0; h0 < H; h0 += 8) {
-#pragma unroll
-                    for (int z = 0; z < 8; ++z) {
-                        t[z] = h0 + z < H ? __ldcg(p.opart + (static_cast<size_t>(h0 + z) * R + i) * d + n)
-                                          : 0.0f;
-                    }
-#pragma unroll
-                    for (int z = 0; z < 8; ++z) {
-                        if (h0 + z < H) o += t[z];
-                    }
-                }
-                o = __fadd_rn(o, __ldg(lw.bo + n));
-                xprime[e] = __fadd_rn(xraw[e], o);
-            }
-        } else if (kind == 2) {
-            if (l + 1 < L) {
-                stage_issue<WT>(lt[l + 1].wqkv, d, cb[kQ0], cb[kQ1], ColMap{d, hd, grp},
-                                lt[l + 1].ln1_g, lt[l + 1].ln1_b, s_stage[0]);
-            } else {
-                stage_issue<WT>(p.head_w, d, cb[kV0], cb[kV1], ColMap{}, p.lnf_g, p.lnf_b, s_stage[0]);
-            }
-            stage_rows(p.ffn, F, R, F, xs);
-            const int n_own = cb[kD1] - cb[kD0];
-            for (int e = threadIdx.x; e < R * n_own; e += kThreads) {
-                const int i = e / n_own, j = e - i * n_own;
-                xown[i * own_ld + j] = xprime[i * d + cb[kD0] + j];
-            }
+    const int hd = d / p.H;
+    const int last = 5 * p.L;
+    for (int phase = 0; phase <= last; ++phase) {
+        const int kind = phase < last ? phase % 5 : 5;
+        const FusedLayer& lw = lt[min(phase / 5, p.L - 1)];
+        if (kind == 1) {
+            attention<KT>(hd, p.q, lw.k_cache, lw.v_cache, s_len, R, p.H, p.slots, p.nchunks,
+                          p.scale, p.part, p.tickets, p.att, qslot);
         } else {
-            stage_rows(p.x, d, R, d, xraw);
-        }
-        // ---- the projection of this phase ----
-        int c0, c1, K = d;
-        ColMap cm{};
-        const void* w;
-        const float* bias;
-        Epi epi;
-        EpiArgs ea;
-        int sidx;
-        switch (kind) {
-            case 0:
-                c0 = cb[kQ0]; c1 = cb[kQ1]; cm = ColMap{d, hd, grp}; w = lw.wqkv; bias = lw.bqkv;
-                epi = Epi::kQkv; sidx = 0;
-                ea.out = p.q; ea.ldo = d; ea.rowmap = s_rows; ea.slot = s_len;
-                ea.k_cache = lw.k_cache; ea.v_cache = lw.v_cache; ea.d = d; ea.heads = H;
-                ea.head_dim = hd; ea.slots = p.slots; ea.kv_bf16 = sizeof(KT) == 2;
-                break;
-            case 1:
-                c0 = cb[kF0]; c1 = cb[kF1]; w = lw.w1; bias = lw.b1; epi = Epi::kGelu; sidx = 1;
-                ea.out = p.ffn; ea.ldo = F;
-                break;
-            case 2:
-                c0 = cb[kD0]; c1 = cb[kD1]; K = F; w = lw.w2; bias = lw.b2; epi = Epi::kResidual;
-                sidx = 2;
-                ea.out = p.x; ea.ldo = d;
-                break;
-            default:
-                c0 = cb[kV0]; c1 = cb[kV1]; w = p.head_w; bias = p.head_b; epi = Epi::kLogits;
-                sidx = 0;
-                ea.out = p.logits; ea.ldo = p.V;
-                break;
-        }
-        __syncthreads();
-        if (c1 > c0) {
-            if (kind != 2) {
-                // The projection's input: LayerNorm of x (A, head: published statistics after the
-                // first layer) or of x' (B: computed here over the whole row).
-                stage_wait(s_stage[sidx], p.err, &abort_flag);
-                const bool use_stats = kind == 3 || (kind == 0 && l > 0);
-                normalise_rows<RT>(kind == 1 ? xprime : xraw, R, d, use_stats ? p.stats : nullptr,
-                                   p.eps, s_stage[sidx].lnp, xs);
+            const ProjDesc pd = describe(p, lt, phase);
+            EpiArgs ea;
+            ea.out = kind == 0 ? p.q : kind == 3 ? p.ffn : kind == 5 ? p.logits : p.x;
+            ea.ldo = kind == 3 ? F : kind == 5 ? p.V : d;
+            ea.rowmap = s_rows;
+            ea.slot = s_len;
+            ea.k_cache = lw.k_cache;
+            ea.v_cache = lw.v_cache;
+            ea.d = d;
+            ea.heads = p.H;
+            ea.head_dim = hd;
+            ea.slots = p.slots;
+            ea.kv_bf16 = sizeof(KT) == 2;
+            // LayerNorm inputs after a residual phase use its published statistics; layer 0's
+            // input comes from the embedding every CTA computed itself.
+            gemv<WT, RT>(pd.x, pd.ldx, phase == 0, pd.ln_g != nullptr, phase > 0, pd.w,
+                         pd.bias != nullptr, pd.N, pd.K, pd.epi, ea, sk, cx, st);
+            if (kind == 2 || kind == 4) {
+                __syncthreads();
+                publish_stats(xown, own_ld, dc1 - dc0, R, p.stats);
             }
-            gemv<WT, RT>(xs, R, K, c0, c1, cm, w, bias, epi, ea, sk, cb[kD0], s_stage[sidx], p.err,
-                         &abort_flag);
         }
-        // ---- after the projection ----
-        if (kind == 0 && grp >= 0) {
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                atom_add_acq_rel(head_arrive + grp, 1);
-                spin_until(head_arrive + grp, arrive_base + static_cast<unsigned>((l + 1) * cph),
-                           p.err, 13, &abort_flag);
-            }
-            __syncthreads();
-            const int warp = threadIdx.x >> 5;
-            attention<KT>(hd, grp, warp * cph + mem, cph * kWarps, p.q, lw.k_cache, lw.v_cache,
-                          s_len, R, H, p.slots, p.nchunks, p.scale, p.part, p.tickets, p.att,
-                          head_merged + grp, qslot);
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                spin_until(head_merged + grp, merged_base + static_cast<unsigned>((l + 1) * R),
-                           p.err, 13, &abort_flag);
-            }
-            __syncthreads();
-            for (int e = threadIdx.x; e < R * hd; e += kThreads) {
-                const int i = e / hd, k = e - i * hd;
-                s_att[e] = __ldcg(p.att + static_cast<size_t>(i) * d + grp * hd + k);
-            }
-            __syncthreads();
-            head_output_block<WT, RT>(s_att, R, hd, grp, d, cb[kO0], cb[kO1],
-                                      static_cast<const WT*>(lw.wo), wpre,
-                                      p.opart + static_cast<size_t>(grp) * R * d);
-        } else if (kind == 2) {
-            __syncthreads();
-            publish_stats(xown, own_ld, cb[kD1] - cb[kD0], R, p.stats);
+        if (phase == last) break;
+        if (kind != 0) {  // the next phase is a projection: stage its weights before the barrier
+            const ProjDesc nd = describe(p, lt, phase + 1);
+            stage_issue<WT>(nd.w, nd.bias, nd.N, nd.K, nd.ln_g, nd.ln_b, st);
         }
-        if (kind == 3) break;
         if (!grid_sync(gsync)) return;
     }
 
@@ -1041,7 +859,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
         const unsigned long long b = atomicExch(p.best + i, 0ull);
         const float first = __ldcg(p.logits + static_cast<size_t>(i) * p.V);
         int token = 0;
-        if (!isnan(first) && b != 0ull) token = unpack_best_index(b);
+        if (!isnan(first) && b != 0ull) token = static_cast<int>(0xffffffffu - static_cast<unsigned>(b));
         s_token[i] = token;
     }
     __syncthreads();
@@ -1067,51 +885,35 @@ __global__ __launch_bounds__(kThreads, 1) void k_decode_step(FusedStep p,
     }
 }
 
-// Shared-memory layout of one CTA: activations, LayerNorm parameters and residual columns
-// (floats), the layer table, then the three weight stages (A: a head's QKV slice, later the head
-// projection; B: FFN1; C: FFN2), each as large as its rows need within the remaining budget.
+// Shared-memory layout of one CTA: activations, LayerNorm parameters, residual columns and bias
+// (floats), the layer table, then the weight stage (the rest of the budget, at most kStageMax).
 struct Layout {
     size_t table_offset = 0;
     size_t stage_offset = 0;
-    unsigned stage_a = 0, stage_b = 0, stage_c = 0;
+    unsigned stage_bytes = 0;
     size_t total = 0;
     bool ok = false;
 };
 
-Layout fused_layout(int R, int d, int F, int V, int L, int H, int ctas, int wbytes) {
+Layout fused_layout(int R, int d, int F, int V, int L, int ctas) {
     Layout lay;
-    if (H < 1 || ctas < H) return lay;
     const size_t own_ld = (d + ctas - 1) / ctas;
-    const size_t floats = static_cast<size_t>(R) * (std::max(d, F) + 2 * d) + 4 * d +
-                          (R * own_ld + 3) / 4 * 4;
+    const size_t widest = std::max({static_cast<size_t>(3) * d, static_cast<size_t>(F),
+                                    static_cast<size_t>(V)});
+    const size_t bias_cap = ((widest + ctas - 1) / ctas + 3) / 4 * 4 + 4;
+    const size_t floats = static_cast<size_t>(R) * (std::max(d, F) + d) + 2 * d +
+                          (R * own_ld + 3) / 4 * 4 + bias_cap;
     lay.table_offset = (floats * sizeof(float) + 15) / 16 * 16;
     lay.stage_offset = (lay.table_offset + sizeof(FusedLayer) * L + 127) / 128 * 128;
     if (lay.stage_offset > kSmemLimit) return lay;
-    const int cph = ctas / H, hd = d / H;
-    auto up = [](size_t x) { return (x + 15) / 16 * 16; };
-    const size_t need_a = up(std::max(static_cast<size_t>((3 * hd + cph - 1) / cph),
-                                      static_cast<size_t>((V + ctas - 1) / ctas)) * d * wbytes);
-    const size_t need_b = up(static_cast<size_t>((F + ctas - 1) / ctas) * d * wbytes);
-    const size_t need_c = up(static_cast<size_t>((d + ctas - 1) / ctas) * F * wbytes);
-    const size_t room = (kSmemLimit - lay.stage_offset) / 16 * 16;
-    const size_t need = need_a + need_b + need_c;
-    if (need <= room) {
-        lay.stage_a = static_cast<unsigned>(need_a);
-        lay.stage_b = static_cast<unsigned>(need_b);
-        lay.stage_c = static_cast<unsigned>(need_c);
-    } else {
-        // Proportional shares, whole 16-byte units; the rows beyond come from global memory.
-        lay.stage_a = static_cast<unsigned>(room * need_a / need / 16 * 16);
-        lay.stage_b = static_cast<unsigned>(room * need_b / need / 16 * 16);
-        lay.stage_c = static_cast<unsigned>(room * need_c / need / 16 * 16);
-    }
-    lay.total = lay.stage_offset + lay.stage_a + lay.stage_b + lay.stage_c;
+    lay.stage_bytes = static_cast<unsigned>(std::min(kStageMax, kSmemLimit - lay.stage_offset) / 16 * 16);
+    lay.total = lay.stage_offset + lay.stage_bytes;
     lay.ok = true;
     return lay;
 }
 
 template <typename WT, typename KT, int RT>
-int prepare_typed(int R, int d, int F, int V, int L, int H) {
+int prepare_typed(int R, int d, int F, int V, int L) {
     auto kernel = k_decode_step<WT, KT, RT>;
     int device = 0, sms = 0, coop = 0;
     if (cudaGetDevice(&device) != cudaSuccess ||
@@ -1120,7 +922,7 @@ int prepare_typed(int R, int d, int F, int V, int L, int H) {
         cudaGetLastError();
         return 0;
     }
-    const Layout lay = fused_layout(R, d, F, V, L, H, sms, sizeof(WT));
+    const Layout lay = fused_layout(R, d, F, V, L, sms);
     if (!coop || !lay.ok || sms > 256) return 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemLimit)) != cudaSuccess) {
@@ -1137,12 +939,11 @@ int prepare_typed(int R, int d, int F, int V, int L, int H) {
 }
 
 template <typename WT, typename KT, int RT>
-cudaError_t launch_typed(cudaStream_t s, const FusedStep& p, const FusedLayer* layers, int ctas,
-                         size_t smem) {
+cudaError_t launch_typed(cudaStream_t s, const FusedStep& p, const FusedLayer* layers, int ctas) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ctas);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = p.wstage_offset + p.wstage_bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -1153,9 +954,9 @@ cudaError_t launch_typed(cudaStream_t s, const FusedStep& p, const FusedLayer* l
 }
 
 struct Prepare {
-    int R, d, F, V, L, H;
+    int R, d, F, V, L;
     template <typename WT, typename KT, int RT>
-    int run() const { return prepare_typed<WT, KT, RT>(R, d, F, V, L, H); }
+    int run() const { return prepare_typed<WT, KT, RT>(R, d, F, V, L); }
 };
 
 struct Launch {
@@ -1163,9 +964,8 @@ struct Launch {
     const FusedStep& p;
     const FusedLayer* layers;
     int ctas;
-    size_t smem;
     template <typename WT, typename KT, int RT>
-    cudaError_t run() const { return launch_typed<WT, KT, RT>(s, p, layers, ctas, smem); }
+    cudaError_t run() const { return launch_typed<WT, KT, RT>(s, p, layers, ctas); }
 };
 
 // fn.run<WT, KT, RT>() for the runtime weight type, cache type and row count (RT = 1 for one row,
@@ -1197,24 +997,22 @@ bool fused_decode_supported(int R, int d, int F, int W, int hd, int w_bf16) {
 }
 
 int fused_decode_prepare(int R, int d, int F, int V, int L, int hd, int w_bf16, int kv_bf16) {
-    return dispatch(w_bf16, kv_bf16, R, Prepare{R, d, F, V, L, d / hd});
+    (void)hd;
+    return dispatch(w_bf16, kv_bf16, R, Prepare{R, d, F, V, L});
 }
 
-int fused_decode_barriers(int layers) { return 3 * layers; }
+int fused_decode_barriers(int layers) { return 5 * layers; }
 
 cudaError_t launch_decode_fused(cudaStream_t s, const FusedStep& step, const FusedLayer* layers,
                                 int w_bf16, int kv_bf16, int hd, int ctas) {
     (void)hd;
-    const Layout lay = fused_layout(step.R, step.d, step.F, step.V, step.L, step.H, ctas,
-                                    w_bf16 ? 2 : 4);
+    const Layout lay = fused_layout(step.R, step.d, step.F, step.V, step.L, ctas);
     if (!lay.ok) return cudaErrorInvalidValue;
     FusedStep p = step;
     p.table_offset = static_cast<unsigned>(lay.table_offset);
     p.wstage_offset = static_cast<unsigned>(lay.stage_offset);
-    p.wstage_a = lay.stage_a;
-    p.wstage_b = lay.stage_b;
-    p.wstage_c = lay.stage_c;
-    return dispatch(w_bf16, kv_bf16, p.R, Launch{s, p, layers, ctas, lay.total});
+    p.wstage_bytes = lay.stage_bytes;
+    return dispatch(w_bf16, kv_bf16, p.R, Launch{s, p, layers, ctas});
 }
 
 }  // namespace bst

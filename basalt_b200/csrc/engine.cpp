@@ -465,8 +465,6 @@ struct Workspace {
     unsigned long long* best = nullptr;       // fused decode step: per-row packed maximum [8]
     double* fused_stats = nullptr;            // fused decode step: LayerNorm statistics [8][256][2]
     bst::FusedLayer* fused_layers = nullptr;  // fused decode step: per-layer table [L]
-    float* fused_opart = nullptr;             // fused decode step: [H][8][d] head partials
-    unsigned* fused_heads = nullptr;          // fused decode step: [2H] head-group counters
     void *k_cache = nullptr, *v_cache = nullptr;
     size_t kv_layer_elems = 0;
     uint64_t generation = 0;
@@ -530,7 +528,6 @@ class Engine {
     // selection reads that instead of scanning the logits.
     bool head_argmax = false;
     unsigned fused_bar_base = 0;         // the fused step's barrier count on the device
-    unsigned fused_launches = 0;         // fused steps launched in the current run
     std::vector<bst::FusedLayer> fused_table;
 
     bool profiling = false;
@@ -975,8 +972,6 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
             sizeof(float) * static_cast<size_t>(rows) * H * splits * (hd + 2));
         add(reinterpret_cast<void**>(&ws.attn_tickets), sizeof(int) * static_cast<size_t>(rows) * H);
         add(reinterpret_cast<void**>(&ws.fused_layers), sizeof(bst::FusedLayer) * L);
-        add(reinterpret_cast<void**>(&ws.fused_opart), sizeof(float) * static_cast<size_t>(H) * 8 * d);
-        add(reinterpret_cast<void**>(&ws.fused_heads), sizeof(unsigned) * 2 * static_cast<size_t>(H));
         ws.kv_layer_elems = static_cast<size_t>(rows) * H * slots * hd;
         const size_t kvb = (kvbf16 ? 2 : 4) * ws.kv_layer_elems * L;
         add(&ws.k_cache, kvb);
@@ -1549,9 +1544,7 @@ int Engine::prepare_fused(int rows) {
                                       sizeof(bst::FusedLayer) * L, cudaMemcpyHostToDevice, stream);
     if (!err) err = cudaMemsetAsync(ws.bar, 0, 2 * sizeof(unsigned), stream);
     if (!err) err = cudaMemsetAsync(ws.best, 0, 8 * sizeof(unsigned long long), stream);
-    if (!err) err = cudaMemsetAsync(ws.fused_heads, 0, 2 * sizeof(unsigned) * H, stream);
     fused_bar_base = 0;
-    fused_launches = 0;
     if (err) {
         cuda_fail(err, "preparing the fused decode step");
         return -1;
@@ -1600,9 +1593,6 @@ int Engine::enqueue_fused(int rows, int steps, const std::vector<int>& lens, boo
     p.err = ws.err;
     p.stats = ws.fused_stats;
     p.history = history ? ws.history : nullptr;
-    p.opart = ws.fused_opart;
-    p.head_ctr = ws.fused_heads;
-    p.launch_index = fused_launches;
     if (p.nchunks > ws.splits) return fail(BST_PANIC, "decode chunk count exceeds the workspace");
     // Algorithmic bytes: every weight once, the cache rows attended, activations are negligible.
     double sum_len = 0;
@@ -1615,7 +1605,6 @@ int Engine::enqueue_fused(int rows, int steps, const std::vector<int>& lens, boo
     });
     if (err) return cuda_fail(err, "fused decode step");
     fused_bar_base += static_cast<unsigned>(fused_ctas) * bst::fused_decode_barriers(L);
-    ++fused_launches;
     return BST_OK;
 }
 

@@ -19,7 +19,6 @@
 #include <math.h>
 #include <stdint.h>
 
-#include <cstdlib>
 #include <mutex>
 
 namespace bst {
@@ -768,197 +767,6 @@ __global__ __launch_bounds__(128) void k_attn_decode(
 }
 
 // ---------------------------------------------------------------------------------------------
-// Decode attention in one pass over the cached keys (the default). Same grid, inputs and outputs
-// as k_attn_decode, but K and V of a key are loaded together and folded into an online softmax,
-// so every round's loads (UK key groups x (K + V) x 16 bytes per lane) are in flight at once; the
-// register budget keeps seven CTAs per SM, so a 1024-CTA launch is one wave; and the
-// kernel never waits between a score pass and a value pass. The CTA's keys are dealt to S
-// streams (LPK lanes each hold one key's 16-byte slices); each stream keeps a running maximum,
-// sum and output slice, and the streams are combined in stream order at the end. The exponent
-// reference differs from the two-pass kernel's single maximum, so results agree with it to
-// rounding, not bit for bit.
-// ---------------------------------------------------------------------------------------------
-template <typename KT, int HD>
-__global__ __launch_bounds__(128, 7) void k_attn_decode_1p(
-    const float* __restrict__ q, const KT* __restrict__ kc, const KT* __restrict__ vc,
-    const int* __restrict__ rowmap, const int* __restrict__ len, int heads, int slots,
-    float scale, int splits, int chunk, float* __restrict__ part, int* __restrict__ tickets,
-    float* __restrict__ out, PlaneOut po, QkvParts qp) {
-    constexpr int EPV = Vec16<KT>::N;  // elements per 16-byte vector
-    constexpr int LPK = HD / EPV;      // lanes per key
-    constexpr int KPW = 32 / LPK;      // keys per warp per key group
-    constexpr int S = 4 * KPW;         // streams per CTA
-    constexpr int UK = 2;              // key groups per round (64 B of K and V per lane)
-    pdl_trigger();
-    pdl_wait();
-    const int i = blockIdx.x / heads, h = blockIdx.x % heads, sp = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row = rowmap[i];
-    const int T = len[row];
-    const int start = sp * chunk, end = min(T, start + chunk);
-    const int n = max(0, end - start);
-    const int d = heads * HD;
-    __shared__ __align__(16) float qs[HD];
-    __shared__ __align__(16) float knew[HD], vnew[HD];
-    __shared__ float sm_m[S], sm_l[S];
-    __shared__ __align__(16) float sm_o[S][HD];
-    __shared__ int s_last;
-    const size_t base = (static_cast<size_t>(row) * heads + h) * slots + start;
-    const unsigned long long pol = evict_first_policy();
-    // With the QKV partial sums, the split holding slot T - 1 (this step's own token) takes that
-    // key and value from shared memory and appends them to the cache; it never reads the slot
-    // back, so every cache read stays on the read-only path.
-    const bool owner = qp.part && n > 0 && end == T;
-    const int n_glob = owner ? n - 1 : n;  // keys read from the cache
-    if (qp.part) {
-        const int R = gridDim.x / heads;
-        const size_t plane = static_cast<size_t>(R) * 3 * d;
-        const float* src = qp.part + static_cast<size_t>(i) * 3 * d;
-        for (int e = tid; e < (owner ? 3 : 1) * HD; e += 128) {
-            const int which = e / HD, ee = e - which * HD;
-            const int col = which * d + h * HD + ee;
-            float t[8];
-#pragma unroll
-            for (int z = 0; z < 8; ++z) t[z] = z < qp.splits ? __ldcg(src + z * plane + col) : 0.0f;
-            float v = 0.0f;
-#pragma unroll
-            for (int z = 0; z < 8; ++z) {
-                if (z < qp.splits) v += t[z];
-            }
-            for (int z = 8; z < qp.splits; ++z) v += __ldcg(src + z * plane + col);
-            if (qp.bias) v = __fadd_rn(v, qp.bias[col]);
-            if (which == 0) {
-                qs[ee] = v;
-            } else {
-                KT* dst = const_cast<KT*>(which == 1 ? kc : vc) + (base + (n - 1)) * HD + ee;
-                float stored;
-                if constexpr (sizeof(KT) == 2) {
-                    *dst = __float2bfloat16_rn(v);
-                    stored = __bfloat162float(*dst);
-                } else {
-                    *dst = v;
-                    stored = v;
-                }
-                (which == 1 ? knew : vnew)[ee] = stored;
-            }
-        }
-    } else {
-        for (int e = tid; e < HD; e += 128) qs[e] = q[static_cast<size_t>(i) * d + h * HD + e];
-    }
-    __syncthreads();
-    const int sub = lane % LPK;              // this lane's 16-byte slice of a key row
-    const int stream = warp * KPW + lane / LPK;
-    float qv[EPV];
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) qv[c] = qs[sub * EPV + c];
-    float m = -INFINITY, l = 0.0f;
-    float o[EPV];
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) o[c] = 0.0f;
-    for (int j0 = stream; j0 < n; j0 += S * UK) {
-        float kv[UK][EPV], vv[UK][EPV];
-#pragma unroll
-        for (int u = 0; u < UK; ++u) {
-            const int j = j0 + u * S;
-            if (j < n_glob) {
-                load16_stream(kc + (base + j) * HD + sub * EPV, kv[u], pol);
-                load16_stream(vc + (base + j) * HD + sub * EPV, vv[u], pol);
-            } else {
-#pragma unroll
-                for (int c = 0; c < EPV; ++c) {
-                    kv[u][c] = j < n ? knew[sub * EPV + c] : 0.0f;
-                    vv[u][c] = j < n ? vnew[sub * EPV + c] : 0.0f;
-                }
-            }
-        }
-        float sc[UK];
-        float mx = m;
-#pragma unroll
-        for (int u = 0; u < UK; ++u) {
-            float dot = 0.0f;
-#pragma unroll
-            for (int c = 0; c < EPV; ++c) dot = fmaf(kv[u][c], qv[c], dot);
-#pragma unroll
-            for (int off = LPK / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(kFull, dot, off);
-            sc[u] = j0 + u * S < n ? __fmul_rn(dot, scale) : -INFINITY;
-            mx = fmaxf(mx, sc[u]);
-        }
-        // Rescale what the stream holds to the new maximum (nothing held yet: factor 0).
-        const float carry = m == -INFINITY ? 0.0f : expf(m - mx);
-        l *= carry;
-#pragma unroll
-        for (int c = 0; c < EPV; ++c) o[c] *= carry;
-#pragma unroll
-        for (int u = 0; u < UK; ++u) {
-            const float pu = sc[u] == -INFINITY ? 0.0f : expf(sc[u] - mx);
-            l += pu;
-#pragma unroll
-            for (int c = 0; c < EPV; ++c) o[c] = fmaf(pu, vv[u][c], o[c]);
-        }
-        m = mx;
-    }
-    if (sub == 0) {
-        sm_m[stream] = m;
-        sm_l[stream] = l;
-    }
-#pragma unroll
-    for (int c = 0; c < EPV; ++c) sm_o[stream][sub * EPV + c] = o[c];
-    __syncthreads();
-    // Streams combined in stream order; thread e < HD owns output dimension e.
-    float M = -INFINITY;
-#pragma unroll
-    for (int z = 0; z < S; ++z) M = fmaxf(M, sm_m[z]);
-    for (int e = tid; e < HD; e += 128) {
-        float L = 0.0f, O = 0.0f;
-#pragma unroll
-        for (int z = 0; z < S; ++z) {
-            if (sm_m[z] == -INFINITY) continue;
-            const float wz = expf(sm_m[z] - M);
-            L = fmaf(sm_l[z], wz, L);
-            O = fmaf(sm_o[z][e], wz, O);
-        }
-        if (splits == 1) {
-            const size_t at = static_cast<size_t>(i) * d + h * HD + e;
-            if (out) out[at] = O / L;
-            if (po.planes) store_split(O / L, po.planes, po.hi, po.lo, at);
-        } else {
-            float* mine = part + (static_cast<size_t>(i * heads + h) * splits + sp) * (HD + 2);
-            mine[e] = O;
-            if (e == 0) {
-                mine[HD] = n > 0 ? M : -INFINITY;
-                mine[HD + 1] = n > 0 ? L : 0.0f;
-            }
-        }
-    }
-    if (splits == 1) return;
-    // Several splits: the last split of the head to finish merges all of them in split order and
-    // re-arms the ticket.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&tickets[i * heads + h], 1) == splits - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const float* all = part + static_cast<size_t>(i * heads + h) * splits * (HD + 2);
-    float MM = -INFINITY;
-    for (int z = 0; z < splits; ++z) MM = fmaxf(MM, __ldcg(all + z * (HD + 2) + HD));
-    for (int e = tid; e < HD; e += 128) {
-        float L = 0.0f, O = 0.0f;
-        for (int z = 0; z < splits; ++z) {
-            const float mz = __ldcg(all + z * (HD + 2) + HD);
-            if (mz == -INFINITY) continue;
-            const float wgt = expf(mz - MM);
-            L = fmaf(__ldcg(all + z * (HD + 2) + HD + 1), wgt, L);
-            O = fmaf(__ldcg(all + z * (HD + 2) + e), wgt, O);
-        }
-        const size_t at = static_cast<size_t>(i) * d + h * HD + e;
-        if (out) out[at] = O / L;
-        if (po.planes) store_split(O / L, po.planes, po.hi, po.lo, at);
-    }
-    if (tid == 0) tickets[i * heads + h] = 0;
-}
-
-// ---------------------------------------------------------------------------------------------
 // Causal prefill attention over one row's freshly written cache slots. CTA = (segment, head,
 // tile of 64 queries), 256 threads; keys stream through shared memory 64 at a time with an online
 // softmax. Register tiling: thread (ty, tx) = (tid / 16, tid % 16) owns queries 4ty..4ty+3 of the
@@ -1427,17 +1235,7 @@ cudaError_t attn_decode_typed(cudaStream_t s, const float* q, void* kc, void* vc
                               const int* rowmap, const int* len, int R, int heads, int slots,
                               float scale, int splits, int chunk, float* part, int* tickets,
                               float* out, const PlaneOut& po, const QkvParts& qp) {
-    // BST_ATTN_TWO_PASS=1 selects the two-pass kernel (scores, then values) for comparison.
-    static const bool two_pass = [] {
-        const char* env = std::getenv("BST_ATTN_TWO_PASS");
-        return env && env[0] == '1';
-    }();
-    if (two_pass) {
-        return launch_pdl(k_attn_decode<KT, HD>, dim3(R * heads, splits), 128, 0, s, q,
-                          static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len,
-                          heads, slots, scale, splits, chunk, part, tickets, out, po, qp);
-    }
-    return launch_pdl(k_attn_decode_1p<KT, HD>, dim3(R * heads, splits), 128, 0, s, q,
+    return launch_pdl(k_attn_decode<KT, HD>, dim3(R * heads, splits), 128, 0, s, q,
                       static_cast<const KT*>(kc), static_cast<const KT*>(vc), rowmap, len, heads,
                       slots, scale, splits, chunk, part, tickets, out, po, qp);
 }

@@ -240,12 +240,8 @@ struct FusedStep {
     int* err = nullptr;            // non-zero when a grid barrier timed out
     double* stats = nullptr;       // [R][grid][2] per-CTA LayerNorm statistics (grid <= 256)
     float* history = nullptr;      // optional [R, steps, V] logits
-    float* opart = nullptr;        // [H, R, d] per-head partial output projections
-    unsigned* head_ctr = nullptr;  // [2H] head-group counters (only grow within a run)
-    unsigned launch_index = 0;     // fused launches earlier in this run (counter bases)
-    unsigned table_offset = 0;     // layer table in shared memory (set by launch)
-    unsigned wstage_offset = 0;    // weight stages in shared memory (set by launch)
-    unsigned wstage_a = 0, wstage_b = 0, wstage_c = 0;
+    unsigned table_offset = 0;                     // layer table in shared memory (set by launch)
+    unsigned wstage_offset = 0, wstage_bytes = 0;  // weight stage in shared memory (set by launch)
 };
 
 // True when the fused step handles this shape (R <= 8, head_dim 32/64/128, window <= 4096).
@@ -254,8 +250,7 @@ bool fused_decode_supported(int R, int d, int F, int W, int head_dim, int w_bf16
 // SM), or 0 when its shared memory does not fit or the device cannot co-schedule it. Call outside
 // stream capture.
 int fused_decode_prepare(int R, int d, int F, int V, int L, int head_dim, int w_bf16, int kv_bf16);
-// Grid barriers one launch passes (bar[0] grows by this times the grid size). The launch also
-// needs heads <= grid size (one CTA group per head).
+// Grid barriers one launch passes (bar[0] grows by this times the grid size).
 int fused_decode_barriers(int layers);
 cudaError_t launch_decode_fused(cudaStream_t s, const FusedStep& p, const FusedLayer* layers,
                                 int w_bf16, int kv_bf16, int head_dim, int ctas);

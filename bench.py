@@ -307,6 +307,24 @@ def event_time(stream, fn, reps):
     return float(np.median(times))
 
 
+def prefill_roofline(m, rows, prompt, prefill_ms):
+    """The prefill call (one decoded token) against the tensor peak: the projections' useful flops
+    (2 M N K over every layer, plus the head on each row's last position); fp32 weights run as
+    3xTF32 (three tf32 passes at half the bf16 rate), bf16 weights as two bf16 passes."""
+    _, bf16_peak, peak_src = measured_peaks()
+    tokens = rows * prompt
+    d, F = m.dimension, m.hidden
+    flops = 2.0 * tokens * m.layers * (4 * d * d + 2 * d * F) + 2.0 * rows * d * m.vocabulary
+    passes, rate = (2, 1.0) if m.weight_dtype == "bf16" else (3, 0.5)
+    achieved = flops / (prefill_ms / 1000.0) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
+            "frac": achieved / bf16_peak, "tensor_passes": passes,
+            "useful_flops_peak": bf16_peak * rate / passes,
+            "useful_frac": achieved / (bf16_peak * rate / passes), "tokens": tokens,
+            "note": "whole prefill call (projections, attention, LayerNorms) against the "
+                    "projections' flops", "peak_source": peak_src}
+
+
 def batch1(local, steps, warmup, tmpdir):
     """Single-stream latency: batch 1, 512-token prompt, 512 greedy tokens (bf16 weights)."""
     import torch
@@ -401,6 +419,8 @@ def other_configs(local, tmpdir, reps=3):
                      "prefill_ms": first_ms, "decode_ms_per_step": decode_ms,
                      "tokens_per_s": w.rows * w.steps / (full_ms / 1000.0),
                      "decode_tokens_per_s": w.rows / (decode_ms / 1000.0) if decode_ms > 0 else None}
+        if w.rows * w.prompt >= 4096:
+            out[name]["roofline_prefill"] = prefill_roofline(m, w.rows, w.prompt, first_ms)
         engine.close()
     return out
 
@@ -578,20 +598,7 @@ def main():
                 if traffic and R == 256 else None,
                 "kernel": "decode step (CUDA graph of the step's kernels)",
                 "algorithmic_bytes": step_bytes, "ms": decode_ms, "peak_source": peak_src}
-    # Prefill: the projections' useful flops (2 M N K over every layer and the head's last rows)
-    # against the tensor peak; fp32 weights run as 3xTF32 (three tf32 passes at half the bf16
-    # rate), bf16 weights as two bf16 passes.
-    tokens = R * workload.prompt
-    d, F = m.dimension, m.hidden
-    prefill_flops = 2.0 * tokens * m.layers * (4 * d * d + 2 * d * F) + 2.0 * R * d * m.vocabulary
-    passes, rate = (2, 1.0) if m.weight_dtype == "bf16" else (3, 0.5)
-    prefill_tflops = prefill_flops / (prefill_ms / 1000.0) / 1e12
-    prefill_roof = {"bound": "tensor", "achieved": prefill_tflops, "peak": bf16_peak,
-                    "unit": "TFLOP/s", "frac": prefill_tflops / bf16_peak,
-                    "tensor_passes": passes, "useful_flops_peak": bf16_peak * rate / passes,
-                    "useful_frac": prefill_tflops / (bf16_peak * rate / passes),
-                    "note": "whole prefill call (projections, attention, LayerNorms) against "
-                            "the projections' flops", "peak_source": peak_src}
+    prefill_roof = prefill_roofline(m, R, workload.prompt, prefill_ms)
 
     line = {
         "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
