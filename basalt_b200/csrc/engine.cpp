@@ -1295,11 +1295,11 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
                                                        ws.next, ws.len, ws.slot, ws.x, R, d);
                    }), "embedding");
     if (st) return st;
-    // Lanes: BST_DECODE_LANES (1, 2 or 4) in the environment, 2 by default; each lane needs more
+    // Lanes: BST_DECODE_LANES (1 to 4) in the environment, 2 by default; each lane needs more
     // than 8 rows (the tensor-core path).
     int nl = 2;
     if (const char* env = std::getenv("BST_DECODE_LANES")) nl = std::atoi(env);
-    nl = nl >= 4 ? 4 : nl >= 2 ? 2 : 1;
+    nl = std::max(1, std::min(nl, kLanes));
     while (nl > 1 && (R / nl <= 8 || !ws.lane_part[nl - 1] ||
                       !linear_on_tc(layers[0].wqkv, R / nl, 3 * d, d))) {
         nl /= 2;
