@@ -769,43 +769,65 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int 
     const float b = bias && n < N ? bias[n] : 0.0f;  // a weight: read before the wait
     pdl_trigger();
     pdl_wait();
-    // The logits epilogue folds the row's argmax: a warp's packed maximum, one atomic per warp, so
-    // every lane stays in the loop (lanes past N contribute nothing).
-    if (E != Epi::kLogits || ea.best == nullptr) {
-        if (n >= N) return;
-    }
+    if (n >= N) return;
     for (int m = blockIdx.y; m < M; m += gridDim.y) {
         const size_t e = static_cast<size_t>(m) * N + n;
+        // Up to 8 splits' loads in flight, then summed in split order.
+        float t[8];
+#pragma unroll
+        for (int z = 0; z < 8; ++z) t[z] = z < splits ? part[static_cast<size_t>(z) * total + e] : 0.0f;
         float v = 0.0f;
-        if (n < N) {
-            // Up to 8 splits' loads in flight, then summed in split order.
-            float t[8];
 #pragma unroll
-            for (int z = 0; z < 8; ++z) t[z] = z < splits ? part[static_cast<size_t>(z) * total + e] : 0.0f;
-#pragma unroll
-            for (int z = 0; z < 8; ++z) {
-                if (z < splits) v += t[z];
-            }
-            for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
-            if (bias) v = __fadd_rn(v, b);
+        for (int z = 0; z < 8; ++z) {
+            if (z < splits) v += t[z];
         }
-        if constexpr (E == Epi::kLogits) {
-            if (ea.best) {
-                unsigned long long p = 0ull;
-                if (n < N) {
-                    ea.out[static_cast<size_t>(ea.rowmap[m]) * ea.ldo + n] = v;
-                    if (!isnan(v)) p = pack_best(v, n);
-                }
+        for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
+        epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, b) : v);
+    }
+}
+
+// The split-K fix-up of the head when it folds the argmax: one block per row, so the row's
+// packed first maximum is reduced inside the block and stored with one plain write (no atomics).
+// The sums and the logits it writes are those of k_splitk_reduce<kLogits>.
+__global__ __launch_bounds__(256) void k_splitk_reduce_logits_best(const float* __restrict__ part,
+                                                                   int splits, int M, int N,
+                                                                   const float* __restrict__ bias,
+                                                                   EpiArgs ea) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned long long s_best[8];
+    const int m = blockIdx.x;
+    const size_t total = static_cast<size_t>(M) * N;
+    unsigned long long best = 0ull;
+    float* out = ea.out + static_cast<size_t>(ea.rowmap[m]) * ea.ldo;
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+        const size_t e = static_cast<size_t>(m) * N + n;
+        float t[8];
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long q = __shfl_xor_sync(0xffffffffu, p, o);
-                    p = q > p ? q : p;
-                }
-                if ((threadIdx.x & 31) == 0 && p) atomicMax(ea.best + ea.rowmap[m], p);
-                continue;
-            }
+        for (int z = 0; z < 8; ++z) t[z] = z < splits ? part[static_cast<size_t>(z) * total + e] : 0.0f;
+        float v = 0.0f;
+#pragma unroll
+        for (int z = 0; z < 8; ++z) {
+            if (z < splits) v += t[z];
         }
-        epi_apply<E>(ea, m, n, v);
+        for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
+        if (bias) v = __fadd_rn(v, bias[n]);
+        out[n] = v;
+        if (!isnan(v)) {
+            const unsigned long long p = pack_best(v, n);
+            best = p > best ? p : best;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long q = __shfl_xor_sync(0xffffffffu, best, o);
+        best = q > best ? q : best;
+    }
+    if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = s_best[w] > best ? s_best[w] : best;
+        ea.best[ea.rowmap[m]] = best;
     }
 }
 
@@ -916,6 +938,12 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
                        a1, b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part);
     }
     if (e != cudaSuccess || sk.splits == 1 || sk.defer) return e;
+    if constexpr (E == Epi::kLogits) {
+        if (ea.best) {
+            return launch_pdl(k_splitk_reduce_logits_best, dim3(M), dim3(256), 0, s, sk.part,
+                              sk.splits, M, N, bias, ea);
+        }
+    }
     const dim3 rgrid((N + 255) / 256, std::min(M, std::max(1, 148 * 8 / ((N + 255) / 256))));
     return launch_pdl(k_splitk_reduce<E>, rgrid, dim3(256), 0, s, sk.part, sk.splits, M, N,
                       bias, ea);

@@ -186,3 +186,32 @@ def test_char96_batch32_sampled_subset(runtime, tmp_path):
     out = engine.streamSampled(ctx[0], w.steps, w.temperature, w.k, streamed.append)
     np.testing.assert_array_equal(out, tokens[0])
     assert streamed == list(tokens[0])
+
+
+@pytest.mark.parametrize("rows", [3, 40])
+def test_greedy_selection_rules_on_crafted_head(runtime, tmp_path, rows):
+    # TextEngine.argmax (TextEngine.java:392-400) on the batched path, whose head epilogue folds
+    # each row's first maximum into a packed word (and on the fused step for <= 8 rows): with the
+    # head weights zeroed the logits are the bias, so ties, signed zeros and NaN decide the token.
+    spec = ModelSpec("padded_decoder", 50, 16, 64, 1, 2, 128)
+    engine, oracle = make_pair(runtime, spec, tmp_path / "w.bin", seed=2, stddev=0.05)
+    engine.setParameter("head.weight", np.zeros(64 * 50, np.float32))
+    ctx = left_pad(synthetic_prompts(5, rows, 6, 50), 16, 50)
+    cases = []
+    tie = np.zeros(50, np.float32)
+    tie[[7, 19, 33]] = 2.5                       # three equal maxima: the first wins
+    cases.append((tie, 7))
+    zeros = np.full(50, -1.0, np.float32)
+    zeros[11] = -0.0
+    zeros[4] = 0.0                               # +0 and -0 are equal: index 4 comes first
+    cases.append((zeros, 4))
+    nan0 = np.arange(50, dtype=np.float32)
+    nan0[0] = np.nan                             # NaN at index 0 is never left
+    cases.append((nan0, 0))
+    nanmid = np.arange(50, dtype=np.float32)
+    nanmid[49] = np.nan                          # a later NaN is never chosen
+    cases.append((nanmid, 48))
+    for bias, want in cases:
+        engine.setParameter("head.bias", bias)
+        tokens = engine.generateBatch(ctx, 2)
+        assert (tokens == want).all(), (bias[:8], tokens[:, 0], want)
