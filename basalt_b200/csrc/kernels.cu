@@ -605,23 +605,6 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __shared__ float knew[HD], vnew[HD];
     const bool owner = qp.part && n > 0 && end == T;
     const int n_glob = owner ? n - 1 : n;  // keys read from the cache
-    const int sub = lane % LPK, kk = lane / LPK;
-    // Scores take U key groups per round, their 16-byte loads all in flight before any is used
-    // (32 floats per lane). The cached keys do not depend on this step's projection, so the
-    // first round's loads are issued before the query is assembled and their DRAM round trip
-    // overlaps it.
-    constexpr int U = 32 / EPV;
-    float kv_first[U][EPV];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int j = warp * KPW + u * 4 * KPW + kk;
-        if (j < n_glob) {
-            load16_stream(kc + (base + j) * HD + sub * EPV, kv_first[u], pol);
-        } else {
-#pragma unroll
-            for (int c = 0; c < EPV; ++c) kv_first[u][c] = 0.0f;
-        }
-    }
     if (qp.part) {
         // The QKV projection's split-K fix-up for this (row, head), in split order then the
         // bias (as k_splitk_reduce sums it).
@@ -663,19 +646,17 @@ __global__ __launch_bounds__(128) void k_attn_decode(
         for (int e = tid; e < HD; e += 128) qs[e] = q[static_cast<size_t>(i) * d + h * HD + e];
     }
     __syncthreads();
+    const int sub = lane % LPK, kk = lane / LPK;
+    // Scores: U key groups per round, their 16-byte loads all in flight before any is used
+    // (32 floats per lane).
+    constexpr int U = 32 / EPV;
     for (int j0 = warp * KPW; j0 < n; j0 += 4 * KPW * U) {
         float kv[U][EPV];
-        const bool first = j0 == warp * KPW;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int j = j0 + u * 4 * KPW + kk;
             if (j < n_glob) {
-                if (first) {
-#pragma unroll
-                    for (int c = 0; c < EPV; ++c) kv[u][c] = kv_first[u][c];
-                } else {
-                    load16_stream(kc + (base + j) * HD + sub * EPV, kv[u], pol);
-                }
+                load16_stream(kc + (base + j) * HD + sub * EPV, kv[u], pol);
             } else if (j < n) {
 #pragma unroll
                 for (int c = 0; c < EPV; ++c) kv[u][c] = knew[sub * EPV + c];
@@ -693,20 +674,6 @@ __global__ __launch_bounds__(128) void k_attn_decode(
 #pragma unroll
             for (int o = LPK / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(kFull, dot, o);
             if (sub == 0 && j < n) sc[j] = __fmul_rn(dot, scale);
-        }
-    }
-    // The first round of value loads does not depend on the softmax: issue it before the
-    // softmax's block-wide reductions, so its DRAM round trip overlaps them.
-    constexpr int UV = 32 / DPL < 16 ? 32 / DPL : 16;
-    float vv_first[UV][DPL];
-#pragma unroll
-    for (int u = 0; u < UV; ++u) {
-        const int jj = min(warp + 4 * u, n - 1);
-        if (jj >= 0 && jj < n_glob) {
-            load_row_stream<DPL>(vc + (base + jj) * HD + lane * DPL, vv_first[u], pol);
-        } else {
-#pragma unroll
-            for (int c = 0; c < DPL; ++c) vv_first[u][c] = jj >= 0 ? vnew[lane * DPL + c] : 0.0f;
         }
     }
     __syncthreads();
@@ -728,21 +695,18 @@ __global__ __launch_bounds__(128) void k_attn_decode(
     __syncthreads();
     sum = stat[4] + stat[5] + stat[6] + stat[7];
     // Weighted values: each warp takes every 4th key, UV keys per round with their loads issued
-    // before the multiply-adds (up to 32 floats per lane; the first round's are in flight).
+    // before the multiply-adds (up to 32 floats per lane).
+    constexpr int UV = 32 / DPL < 16 ? 32 / DPL : 16;
     float o[DPL];
 #pragma unroll
     for (int c = 0; c < DPL; ++c) o[c] = 0.0f;
     for (int j0 = warp; j0 < n; j0 += 4 * UV) {
         float vv[UV][DPL];
-        const bool first = j0 == warp;
 #pragma unroll
         for (int u = 0; u < UV; ++u) {
             const int j = j0 + 4 * u;
             const int jj = min(j, n - 1);
-            if (first) {
-#pragma unroll
-                for (int c = 0; c < DPL; ++c) vv[u][c] = vv_first[u][c];
-            } else if (jj < n_glob) {
+            if (jj < n_glob) {
                 load_row_stream<DPL>(vc + (base + jj) * HD + lane * DPL, vv[u], pol);
             } else {
 #pragma unroll
