@@ -2311,11 +2311,14 @@ static int32_t logits_rows_call(bst_engine h, Mode mode, const int32_t* contexts
                 }
             }
         }
+        // The watch list lives for this call only, however it ends.
+        struct WatchScope {
+            std::vector<int32_t>& w;
+            ~WatchScope() { w.clear(); }
+        } scope{e->watch};
         e->watch = std::move(watch);
-        const int st = e->run(mode, contexts, rows, length, steps, temperature, top_k, tokens,
-                              false, nullptr, nullptr, nullptr, logits);
-        e->watch.clear();
-        return set_error(e, st);
+        return set_error(e, e->run(mode, contexts, rows, length, steps, temperature, top_k, tokens,
+                                   false, nullptr, nullptr, nullptr, logits));
     })
 }
 

@@ -207,8 +207,6 @@ struct Context {
 std::mutex g_mutex;
 std::unordered_map<uint64_t, std::shared_ptr<Context>> g_contexts;
 uint64_t g_next_context = 1;
-thread_local std::string t_error;
-
 std::shared_ptr<Context> find_context(bst_context h) {
     std::lock_guard<std::mutex> lock(g_mutex);
     auto it = g_contexts.find(h);
@@ -216,8 +214,7 @@ std::shared_ptr<Context> find_context(bst_context h) {
 }
 
 int unknown_context(bst_context h) {
-    t_error = "context handle " + std::to_string(h) + " is not live";
-    bst::set_thread_error(t_error);
+    bst::set_thread_error("context handle " + std::to_string(h) + " is not live");
     return BST_UNKNOWN_HANDLE;
 }
 
