@@ -52,7 +52,9 @@ CONFIGS = {
                  rows=256, prompt=256, steps=256, prompt_seed=3),
         Workload("v8192-d768-l12-w1024-b1-greedy-bf16w", _C4, rows=1, prompt=512, steps=512,
                  prompt_seed=4),
-        Workload("v8192-d768-l12-w1024-n8192-sampled-bf16w", replace(_C4, max_rows=1024),
+        # 8192 sequences in waves of 2048 rows (~97 GB of fp32 cache at 640 slots): 10 % more
+        # tokens/s than waves of 1024 on one B200, measured.
+        Workload("v8192-d768-l12-w1024-n8192-sampled-bf16w", replace(_C4, max_rows=2048),
                  rows=8192, prompt=128, steps=512, prompt_seed=5, mode="sample",
                  temperature=1.0, sample_seed=9),
     ]

@@ -532,6 +532,18 @@ class Engine {
 
     bool profiling = false;
     bool in_step = false;  // enqueuing a batched decode step (decode_layers)
+    struct StepScope {
+        bool& flag;
+        explicit StepScope(bool& f) : flag(f) { flag = true; }
+        ~StepScope() { flag = false; }
+    };
+    // Lane ring of the batched decode step: with several lanes, each lane's attention kernel
+    // waits for the previous attention in the ring (lane i after lane i - 1 of the same layer,
+    // lane 0 after the last lane of the layer before), so the lanes take turns at streaming the
+    // cache while the others run their projections. decode_layer waits for attn_after (when
+    // set) before its attention and records attn_done after it.
+    cudaEvent_t lane_attn[kLanes] = {};
+    cudaEvent_t attn_after = nullptr, attn_done = nullptr;
     KernelStats stats[bst::kKernelClassCount];
     std::vector<PendingTiming> pending;
     std::vector<cudaEvent_t> event_pool;
@@ -578,6 +590,10 @@ class Engine {
         }
         if (lane_fork) cudaEventDestroy(lane_fork);
         lane_fork = nullptr;
+        for (int i = 0; i < kLanes; ++i) {
+            if (lane_attn[i]) cudaEventDestroy(lane_attn[i]);
+            lane_attn[i] = nullptr;
+        }
     }
 
     // ---- launches with optional per-class timing ----
@@ -659,8 +675,16 @@ class Engine {
     int enqueue_prefill(const StepPlan& p, size_t begin, size_t end);
     int enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens);
     // The layers and head of a decode step for R rows whose embedded inputs are in ws.x, on
-    // `stream` (enqueue_decode runs it once, or once per lane with the workspace views shifted).
+    // `stream` (enqueue_decode runs it once, or runs decode_layer and decode_head per lane with
+    // the workspace views shifted).
+    struct DecodePlan {
+        int splits = 1, chunk = 32;  // decode attention: cache splits per (row, head), keys each
+        double sum_len = 0;          // cached keys over the rows (for the byte counts)
+    };
+    int decode_plan(int R, const std::vector<int>& lens, DecodePlan* dp);
     int decode_layers(int R, const int* rowmap, const std::vector<int>& lens);
+    int decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp, bool* x_normalised);
+    int decode_head(int R, const int* rowmap, bool x_normalised);
     int qkv_partials(const LayerWeights& lw, const bst::LnArgs* ln, int R, int splits);
     int enqueue_direct(int rows);
     int prepare_fused(int rows);
@@ -1306,37 +1330,63 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     }
     if (nl == 1) return decode_layers(R, rowmap, lens);
     // Lane i takes rows [i R / nl, (i + 1) R / nl) with every per-row workspace view shifted to
-    // them; lanes > 0 run on their own streams with private planes and partials. All start
-    // together (starting lanes a layer phase apart, so that attention meets another lane's
-    // projections, measured slower).
+    // them; lanes > 0 run on their own streams with private planes and partials. The lanes are
+    // enqueued layer by layer, so that BST_LANE_RING=1 in the environment can chain their
+    // attention kernels into a ring (see lane_attn).
+    const char* ring_env = std::getenv("BST_LANE_RING");
+    const bool ring = ring_env && std::atoi(ring_env) != 0;
     cudaError_t err = cudaEventRecord(lane_fork, stream);
     for (int i = 1; i < nl && !err; ++i) err = cudaStreamWaitEvent(lane_stream[i], lane_fork, 0);
     if (err) return cuda_fail(err, "forking the decode lanes");
     const Workspace saved = ws;
-    cudaStream_t main = stream;
+    const cudaStream_t main = stream;
+    Workspace lane_ws[kLanes];
+    DecodePlan plan[kLanes];
+    bool normalised[kLanes] = {};
+    int first[kLanes + 1];
+    for (int i = 0; i <= nl; ++i) first[i] = i * R / nl;
     for (int i = 0; i < nl && !st; ++i) {
-        const int r0 = i * R / nl, r1 = (i + 1) * R / nl;
-        ws = saved;
+        const int r0 = first[i];
+        lane_ws[i] = saved;
+        Workspace& w = lane_ws[i];
         if (i > 0) {
-            stream = lane_stream[i];
-            ws.x += static_cast<size_t>(r0) * d;
-            ws.q += static_cast<size_t>(r0) * d;
-            ws.att += static_cast<size_t>(r0) * d;
-            ws.ffn += static_cast<size_t>(r0) * F;
-            ws.slot += r0;
-            ws.attn_tickets += static_cast<size_t>(r0) * H;
-            ws.part += static_cast<size_t>(r0) * H * ws.splits * (hd + 2);
-            ws.xs_hi = ws.lane_xs_hi[i];
-            ws.xs_lo = ws.lane_xs_lo[i];
-            ws.ys_hi = ws.lane_ys_hi[i];
-            ws.ys_lo = ws.lane_ys_lo[i];
-            ws.tc_part = ws.lane_part[i];
+            w.x += static_cast<size_t>(r0) * d;
+            w.q += static_cast<size_t>(r0) * d;
+            w.att += static_cast<size_t>(r0) * d;
+            w.ffn += static_cast<size_t>(r0) * F;
+            w.slot += r0;
+            w.attn_tickets += static_cast<size_t>(r0) * H;
+            w.part += static_cast<size_t>(r0) * H * saved.splits * (hd + 2);
+            w.xs_hi = saved.lane_xs_hi[i];
+            w.xs_lo = saved.lane_xs_lo[i];
+            w.ys_hi = saved.lane_ys_hi[i];
+            w.ys_lo = saved.lane_ys_lo[i];
+            w.tc_part = saved.lane_part[i];
         }
-        st = decode_layers(r1 - r0, rowmap + r0,
-                           std::vector<int>(lens.begin() + r0, lens.begin() + r1));
-        stream = main;
+        st = decode_plan(first[i + 1] - r0,
+                         std::vector<int>(lens.begin() + r0, lens.begin() + first[i + 1]), &plan[i]);
+    }
+    {
+        StepScope scope(in_step);
+        for (int l = 0; l < L && !st; ++l) {
+            for (int i = 0; i < nl && !st; ++i) {
+                ws = lane_ws[i];
+                stream = i ? lane_stream[i] : main;
+                attn_after = ring && (l > 0 || i > 0) ? lane_attn[(i + nl - 1) % nl] : nullptr;
+                attn_done = ring ? lane_attn[i] : nullptr;
+                st = decode_layer(l, first[i + 1] - first[i], rowmap + first[i], plan[i],
+                                  &normalised[i]);
+            }
+        }
+        attn_after = attn_done = nullptr;
+        for (int i = 0; i < nl && !st; ++i) {
+            ws = lane_ws[i];
+            stream = i ? lane_stream[i] : main;
+            st = decode_head(first[i + 1] - first[i], rowmap + first[i], normalised[i]);
+        }
     }
     ws = saved;
+    stream = main;
     if (st) return st;
     for (int i = 1; i < nl && !err; ++i) {
         err = cudaEventRecord(lane_join[i], lane_stream[i]);
@@ -1370,95 +1420,113 @@ int Engine::qkv_partials(const LayerWeights& lw, const bst::LnArgs* ln, int R, i
     return err ? cuda_fail(err, "qkv projection") : BST_OK;
 }
 
-int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens) {
-    // GEMMs enqueued below are profiled as the decode step's (kGemmStep).
-    struct StepScope {
-        bool& flag;
-        explicit StepScope(bool& f) : flag(f) { flag = true; }
-        ~StepScope() { flag = false; }
-    } scope(in_step);
-    const double kvb = kvbf16 ? 2.0 : 4.0;
-    const int slots = ws.slots;
-    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
+int Engine::decode_plan(int R, const std::vector<int>& lens, DecodePlan* dp) {
     // Splits over the cache: enough CTAs for two waves of the SMs, chunks of >= 32 keys. Sized
     // by the run's slot capacity, not this step's lengths, so a captured step graph stays valid
     // as the cache grows; splits past a row's length return at once.
     const int max_len = std::max(1, ws.slots);
-    double sum_len = 0;
-    for (int n : lens) sum_len += n;
+    dp->sum_len = 0;
+    for (int n : lens) dp->sum_len += n;
     int splits = std::max(1, (592 + R * H - 1) / (R * H));
     int chunk = (max_len + splits - 1) / splits;
     chunk = std::max(32, (chunk + 31) / 32 * 32);
     chunk = std::min(chunk, 1024);
     splits = (max_len + chunk - 1) / chunk;
     if (splits > ws.splits) return fail(BST_PANIC, "decode split count exceeds the workspace");
+    dp->splits = splits;
+    dp->chunk = chunk;
+    return BST_OK;
+}
+
+int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens) {
+    // GEMMs enqueued below are profiled as the decode step's (kGemmStep).
+    StepScope scope(in_step);
+    DecodePlan dp;
+    int st = decode_plan(R, lens, &dp);
+    bool x_normalised = false;  // ws.xs_* holds this layer's LN1 (or the final LN) of ws.x
+    for (int l = 0; l < L && !st; ++l) st = decode_layer(l, R, rowmap, dp, &x_normalised);
+    return st ? st : decode_head(R, rowmap, x_normalised);
+}
+
+int Engine::decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp,
+                         bool* x_normalised) {
+    const double kvb = kvbf16 ? 2.0 : 4.0;
+    const int slots = ws.slots;
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
     auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
     int st = BST_OK;
-    bool x_normalised = false;  // ws.xs_* holds this layer's LN1 (or the final LN) of ws.x
-    for (int l = 0; l < L; ++l) {
-        const LayerWeights& lw = layers[l];
-        const bst::LnArgs ln1{lw.ln1_g, lw.ln1_b, kLayerNormEps};
-        EpiArgs qkv;
-        qkv.out = ws.q;
-        qkv.ldo = d;
-        qkv.rowmap = rowmap;
-        qkv.slot = ws.slot;
-        qkv.k_cache = static_cast<char*>(ws.k_cache) + l * ws.kv_layer_elems * static_cast<size_t>(kvb);
-        qkv.v_cache = static_cast<char*>(ws.v_cache) + l * ws.kv_layer_elems * static_cast<size_t>(kvb);
-        qkv.d = d;
-        qkv.heads = H;
-        qkv.head_dim = hd;
-        qkv.slots = slots;
-        qkv.kv_bf16 = kvbf16;
-        // A split-K QKV projection leaves its partial sums to the attention kernel, which sums
-        // q per head and appends the step's key and value to the cache itself.
-        bst::QkvParts qparts;
-        if (linear_on_tc(lw.wqkv, R, 3 * d, d)) {
-            const int qkv_splits = bst::tc_plan(R, 3 * d, d, wbf16, bst::tc_part_bytes_max(), nullptr);
-            if (qkv_splits > 1) qparts = bst::QkvParts{ws.tc_part, qkv_splits, lw.bqkv};
-        }
-        if (qparts.part) {
-            st = qkv_partials(lw, x_normalised ? nullptr : &ln1, R, qparts.splits);
-        } else {
-            st = x_normalised ? linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
-                                       "qkv projection", nullptr, false, true)
-                              : linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
-                                       "qkv projection", &ln1);
-        }
-        if (st) return st;
-        const double kv_bytes = sum_len * 2.0 * d * kvb + R * d * 4.0 +
-                                (qparts.part ? qparts.splits * R * 3.0 * d * 4.0 : 0.0);
-        const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
-        st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * sum_len * d, 1, [&] {
-                       return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
-                                                      kvbf16, rowmap, ws.len, R, H, hd, slots,
-                                                      scale, splits, chunk, ws.part,
-                                                      ws.attn_tickets,
-                                                      att_planes.planes ? nullptr : ws.att,
-                                                      att_planes, qparts);
-                   }), "decode attention");
-        if (st) return st;
-        const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
-        bool ffn_in_normalised = false;
-        st = residual_ln(ws.att, d, lw.wo, lw.bo, R, d, d, att_planes.planes != 0, ln2,
-                         "output projection", &ffn_in_normalised);
-        if (st) return st;
-        EpiArgs act;
-        act.ldo = F;
-        act.split = planes_for(lw.w2, R, d, F);
-        act.out = act.split.planes ? nullptr : ws.ffn;  // FFN2 reads only the planes
-        st = ffn_in_normalised ? linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
-                                        nullptr, false, true)
-                               : linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
-                                        &ln2);
-        if (st) return st;
-        const bst::LnArgs next = l + 1 < L ? bst::LnArgs{layers[l + 1].ln1_g, layers[l + 1].ln1_b,
-                                                         kLayerNormEps}
-                                           : bst::LnArgs{lnf_g, lnf_b, kLayerNormEps};
-        st = residual_ln(ws.ffn, F, lw.w2, lw.b2, R, d, F, act.split.planes != 0, next, "ffn2",
-                         &x_normalised);
+    const LayerWeights& lw = layers[l];
+    const bst::LnArgs ln1{lw.ln1_g, lw.ln1_b, kLayerNormEps};
+    EpiArgs qkv;
+    qkv.out = ws.q;
+    qkv.ldo = d;
+    qkv.rowmap = rowmap;
+    qkv.slot = ws.slot;
+    qkv.k_cache = static_cast<char*>(ws.k_cache) + l * ws.kv_layer_elems * static_cast<size_t>(kvb);
+    qkv.v_cache = static_cast<char*>(ws.v_cache) + l * ws.kv_layer_elems * static_cast<size_t>(kvb);
+    qkv.d = d;
+    qkv.heads = H;
+    qkv.head_dim = hd;
+    qkv.slots = slots;
+    qkv.kv_bf16 = kvbf16;
+    // A split-K QKV projection leaves its partial sums to the attention kernel, which sums
+    // q per head and appends the step's key and value to the cache itself.
+    bst::QkvParts qparts;
+    if (linear_on_tc(lw.wqkv, R, 3 * d, d)) {
+        const int qkv_splits = bst::tc_plan(R, 3 * d, d, wbf16, bst::tc_part_bytes_max(), nullptr);
+        if (qkv_splits > 1) qparts = bst::QkvParts{ws.tc_part, qkv_splits, lw.bqkv};
+    }
+    if (qparts.part) {
+        st = qkv_partials(lw, *x_normalised ? nullptr : &ln1, R, qparts.splits);
+    } else {
+        st = *x_normalised ? linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
+                                    "qkv projection", nullptr, false, true)
+                           : linear(ws.x, d, lw.wqkv, lw.bqkv, R, 3 * d, d, Epi::kQkv, qkv,
+                                    "qkv projection", &ln1);
+    }
+    if (st) return st;
+    const double kv_bytes = dp.sum_len * 2.0 * d * kvb + R * d * 4.0 +
+                            (qparts.part ? qparts.splits * R * 3.0 * d * 4.0 : 0.0);
+    const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
+    if (attn_after) {
+        st = check(cudaStreamWaitEvent(stream, attn_after, 0), "ordering the lanes' attention");
         if (st) return st;
     }
+    st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * dp.sum_len * d, 1, [&] {
+                   return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
+                                                  kvbf16, rowmap, ws.len, R, H, hd, slots,
+                                                  scale, dp.splits, dp.chunk, ws.part,
+                                                  ws.attn_tickets,
+                                                  att_planes.planes ? nullptr : ws.att,
+                                                  att_planes, qparts);
+               }), "decode attention");
+    if (st) return st;
+    if (attn_done) {
+        st = check(cudaEventRecord(attn_done, stream), "ordering the lanes' attention");
+        if (st) return st;
+    }
+    const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
+    bool ffn_in_normalised = false;
+    st = residual_ln(ws.att, d, lw.wo, lw.bo, R, d, d, att_planes.planes != 0, ln2,
+                     "output projection", &ffn_in_normalised);
+    if (st) return st;
+    EpiArgs act;
+    act.ldo = F;
+    act.split = planes_for(lw.w2, R, d, F);
+    act.out = act.split.planes ? nullptr : ws.ffn;  // FFN2 reads only the planes
+    st = ffn_in_normalised ? linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
+                                    nullptr, false, true)
+                           : linear(ws.x, d, lw.w1, lw.b1, R, F, d, Epi::kGelu, act, "ffn1",
+                                    &ln2);
+    if (st) return st;
+    const bst::LnArgs next = l + 1 < L ? bst::LnArgs{layers[l + 1].ln1_g, layers[l + 1].ln1_b,
+                                                     kLayerNormEps}
+                                       : bst::LnArgs{lnf_g, lnf_b, kLayerNormEps};
+    return residual_ln(ws.ffn, F, lw.w2, lw.b2, R, d, F, act.split.planes != 0, next, "ffn2",
+                       x_normalised);
+}
+
+int Engine::decode_head(int R, const int* rowmap, bool x_normalised) {
     const bst::LnArgs lnf{lnf_g, lnf_b, kLayerNormEps};
     EpiArgs lg;
     lg.out = ws.logits;
@@ -2035,6 +2103,9 @@ int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine
             if (!err) err = cudaEventCreateWithFlags(&e->lane_join[i], cudaEventDisableTiming);
         }
         if (!err) err = cudaEventCreateWithFlags(&e->lane_fork, cudaEventDisableTiming);
+        for (int i = 0; i < kLanes && !err; ++i) {
+            err = cudaEventCreateWithFlags(&e->lane_attn[i], cudaEventDisableTiming);
+        }
         if (!err) err = bst::configure_device_kernels_once(device);
         if (err) {
             cudaGetLastError();

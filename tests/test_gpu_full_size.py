@@ -127,15 +127,15 @@ def test_v8192_d768_l12_batch1_greedy_bf16_weights_every_step(runtime, weights):
 
 
 def test_v8192_d768_l12_8192_sequences_sampled_every_draw(runtime, weights):
-    # The 8192-sequence streamSampled workload (T = 1.0, seed 9, 512 tokens) in waves of 1024
-    # rows: rows from four different waves are replayed draw for draw, each from the generator
-    # state one engine seeded once would hold at its first draw (TextEngine.java:43,417).
+    # The 8192-sequence streamSampled workload (T = 1.0, seed 9, 512 tokens) in waves of 2048
+    # rows: rows from all four waves are replayed draw for draw, each from the generator state one
+    # engine seeded once would hold at its first draw (TextEngine.java:43,417).
     w = config("v8192-d768-l12-w1024-n8192-sampled-bf16w")
     m = w.model
     engine, oracle = pair(runtime, w, weights)
     ctx = left_pad(synthetic_prompts(w.prompt_seed, w.rows, w.prompt, m.vocabulary), m.window,
                    m.vocabulary)
-    rows = [0, 1500, 4100, 8191]
+    rows = [0, 2500, 4100, 8191]
     engine.seed(w.sample_seed)
     tokens, logits = engine.sampleWithLogitsOf(ctx, w.steps, w.temperature, w.k, rows)
     assert tokens.shape == (8192, 512) and tokens.min() >= 0 and tokens.max() < m.vocabulary
