@@ -112,6 +112,23 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
         : "memory");
 }
 
+// Tiled bulk store of one box from shared memory into a 3-D tensor (the split-K partials), then
+// the wait until the box has been read out of shared memory. Elements outside the tensor are not
+// written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y,
+                                             int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit_and_drain() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major tile of 128-byte rows with the 128-byte swizzle:
 // 8-row groups 1024 bytes apart (SBO), leading offset unused (1), descriptor version 1.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -395,8 +412,8 @@ template <int FMT, int BN, Epi E, int ST>
 __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
     const __grid_constant__ CUtensorMap a0, const __grid_constant__ CUtensorMap a1,
     const __grid_constant__ CUtensorMap b0, const __grid_constant__ CUtensorMap b1,
-    const float* __restrict__ bias, int M, int N, int K, EpiArgs ea, int* err, int splits,
-    float* __restrict__ part) {
+    const __grid_constant__ CUtensorMap pmap, const float* __restrict__ bias, int M, int N, int K,
+    EpiArgs ea, int* err, int splits, float* __restrict__ part, int part_tma) {
     using C = Config<FMT, BN, ST>;
     constexpr int kSingleTmemCols = BN < 32 ? 32 : BN;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -508,6 +525,44 @@ __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
         const int quarter = warp & 3;
         const bool ok = mbar_wait_tile(acc_full, 0, err, 3);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (part_tma) {
+            // Split-K partials leave through the TMA unit: the tile is staged in the drained
+            // ring as BN / 32 boxes of 128 rows x 128 bytes in the 128-byte swizzle (the 16-byte
+            // chunk q of row r at chunk q ^ (r % 8), so each quarter-warp's vector stores hit
+            // distinct banks), then one thread stores the boxes into part[z] and waits until
+            // they have been read out of shared memory.
+            const bool all_ok = __all_sync(0xffffffffu, ok);
+            if (all_ok) {
+                const int r = quarter * 32 + lane;
+                const uint32_t row_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+                unsigned char* rowp = base + r * kRowBytes;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 16) {
+                    float v[16];
+                    tmem_ld<16>(row_addr + c, v);
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const int col = c + 4 * g;
+                        const int q = (col & 31) >> 2;
+                        float4* dst = reinterpret_cast<float4*>(
+                            rowp + (col >> 5) * (BM * kRowBytes) + ((q ^ (r & 7)) << 4));
+                        *dst = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+                    }
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (threadIdx.x == 64 && all_ok) {
+#pragma unroll
+                for (int j = 0; j < BN / 32; ++j) {
+                    if (n0 + 32 * j < N) {
+                        tma_store_3d(&pmap, base + j * (BM * kRowBytes), n0 + 32 * j, m0,
+                                     blockIdx.z);
+                    }
+                }
+                tma_store_commit_and_drain();
+            }
+        } else {
         // Stage the 128 x BN tile through shared memory (the drained pipeline ring), so the
         // global traffic below is row-coalesced.
         float* tile = reinterpret_cast<float*>(base);
@@ -541,6 +596,7 @@ __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
                     epi_apply<E>(ea, m, n, bias ? __fadd_rn(v, bias[n]) : v);
                 }
             }
+        }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -907,10 +963,27 @@ cudaError_t make_map(CUtensorMap* map, const void* ptr, int rows, int K, bool bf
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// 3-D map over split-K partials part[splits][M][N] (fp32) with a 32-column x 128-row box in the
+// 128-byte swizzle, for the tiled bulk stores of k_gemm_tc. Needs N % 4 == 0 (16-byte strides).
+cudaError_t make_part_map(CUtensorMap* map, float* part, int splits, int M, int N) {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M),
+                          static_cast<cuuint64_t>(splits)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(N) * 4, static_cast<cuuint64_t>(M) * N * 4};
+    cuuint32_t box[3] = {32, static_cast<cuuint32_t>(BM), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 struct SplitK {
     int splits = 1;
     float* part = nullptr;
     bool defer = false;  // leave the split sums to the caller (launch_reduce_residual_ln)
+    CUtensorMap pmap{};  // over part, when tma is set
+    int tma = 0;         // the one-tile kernel stores the partials with the TMA unit
 };
 
 template <int FMT, int BN, Epi E>
@@ -925,12 +998,12 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
     cudaError_t e = cudaSuccess;
     if (units <= resident) {
         e = launch_pdl(k_gemm_tc<FMT, BN, E, 0>, tiles, dim3(kSingleThreads), C::kSmem, s, a0, a1,
-                       b0, b1, bias, M, N, K, ea, err, sk.splits, sk.part);
+                       b0, b1, sk.pmap, bias, M, N, K, ea, err, sk.splits, sk.part, sk.tma);
     } else if (BN == 64 && units <= sms * Config<FMT, BN, 2>::kCtasPerSm) {
         if constexpr (BN == 64) {
             e = launch_pdl(k_gemm_tc<FMT, BN, E, 2>, tiles, dim3(kSingleThreads),
-                           Config<FMT, BN, 2>::kSmem, s, a0, a1, b0, b1, bias, M, N, K, ea, err,
-                           sk.splits, sk.part);
+                           Config<FMT, BN, 2>::kSmem, s, a0, a1, b0, b1, sk.pmap, bias, M, N, K,
+                           ea, err, sk.splits, sk.part, sk.tma);
         }
     } else {
         const dim3 grid(static_cast<unsigned>(std::min<long>(units, resident)));
@@ -1072,6 +1145,10 @@ cudaError_t launch_gemm_tc(cudaStream_t s, const void* x_hi, const void* x_lo, c
     sk.splits = tc_plan(M, N, K, w_bf16, part ? part_bytes : 0, &bn);
     sk.part = part;
     sk.defer = defer_fixup;
+    if (sk.splits > 1 && N % 4 == 0 && (reinterpret_cast<uintptr_t>(part) & 15) == 0) {
+        if ((e = make_part_map(&sk.pmap, part, sk.splits, M, N)) != cudaSuccess) return e;
+        sk.tma = 1;
+    }
     CUtensorMap a0, a1, b0, b1;
     if ((e = make_map(&a0, x_hi, M, K, w_bf16, BM)) != cudaSuccess) return e;
     if ((e = make_map(&a1, x_lo, M, K, w_bf16, BM)) != cudaSuccess) return e;
