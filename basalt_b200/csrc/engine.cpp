@@ -682,7 +682,11 @@ class Engine {
         double sum_len = 0;          // cached keys over the rows (for the byte counts)
     };
     int decode_plan(int R, const std::vector<int>& lens, DecodePlan* dp);
-    int decode_layers(int R, const int* rowmap, const std::vector<int>& lens);
+    int decode_layers(int R, const int* rowmap, const std::vector<int>& lens,
+                      bool x_normalised);
+    // Embeds the step's next token of R rows into ws.x (and with `normalise`, the first
+    // layer's LayerNorm of them into the operand planes ws.xs_*).
+    int embed_rows(int R, const int* rowmap, bool normalise);
     int decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp, bool* x_normalised);
     int decode_head(int R, const int* rowmap, bool x_normalised);
     int qkv_partials(const LayerWeights& lw, const bst::LnArgs* ln, int R, int splits);
@@ -1311,14 +1315,28 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
     return linear(ws.last, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head", &lnf);
 }
 
-int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens) {
+int Engine::embed_rows(int R, const int* rowmap, bool normalise) {
     const double wb = wbf16 ? 2.0 : 4.0;
-    auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
-    int st = check(launch(bst::kEmbed, R * d * (2 * wb + 4.0), 0, 1, [&] {
-                       return bst::launch_embed_decode(stream, tok_emb, pos_emb, wbf16, rowmap,
-                                                       ws.next, ws.len, ws.slot, ws.x, R, d);
-                   }), "embedding");
-    if (st) return st;
+    cudaError_t err;
+    if (normalise) {
+        const double plane = static_cast<double>(bst::tc_split_bytes(R, d, wbf16));
+        err = launch(bst::kEmbed, R * d * (2 * wb + 4.0) + 2 * plane, 0, 1, [&] {
+            return bst::launch_embed_ln_decode(stream, tok_emb, pos_emb, wbf16, rowmap, ws.next,
+                                               ws.len, ws.slot, ws.x, R, d, layers[0].ln1_g,
+                                               layers[0].ln1_b, kLayerNormEps, ws.xs_hi, ws.xs_lo,
+                                               wbf16 ? 2 : 1);
+        });
+    } else {
+        err = launch(bst::kEmbed, R * d * (2 * wb + 4.0), 0, 1, [&] {
+            return bst::launch_embed_decode(stream, tok_emb, pos_emb, wbf16, rowmap, ws.next,
+                                            ws.len, ws.slot, ws.x, R, d);
+        });
+    }
+    return err ? cuda_fail(err, "embedding") : BST_OK;
+}
+
+int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& lens) {
+    int st = BST_OK;
     // Lanes: BST_DECODE_LANES (1 to 4) in the environment, 2 by default; each lane needs more
     // than 8 rows (the tensor-core path).
     int nl = 2;
@@ -1328,7 +1346,13 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
                       !linear_on_tc(layers[0].wqkv, R / nl, 3 * d, d))) {
         nl /= 2;
     }
-    if (nl == 1) return decode_layers(R, rowmap, lens);
+    if (nl == 1) {
+        // On the tensor-core path the embedding kernel also writes the first LayerNorm's
+        // operand planes; the GEMV path normalises inside its own projection.
+        const bool normalise = linear_on_tc(layers[0].wqkv, R, 3 * d, d) && d <= 1024;
+        st = embed_rows(R, rowmap, normalise);
+        return st ? st : decode_layers(R, rowmap, lens, normalise);
+    }
     // Lane i takes rows [i R / nl, (i + 1) R / nl) with every per-row workspace view shifted to
     // them; lanes > 0 run on their own streams with private planes and partials. The lanes are
     // enqueued layer by layer, so that BST_LANE_RING=1 in the environment can chain their
@@ -1365,6 +1389,14 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
         }
         st = decode_plan(first[i + 1] - r0,
                          std::vector<int>(lens.begin() + r0, lens.begin() + first[i + 1]), &plan[i]);
+    }
+    // Each lane embeds its own rows and writes the first LayerNorm's operand planes.
+    const bool normalise = d <= 1024;
+    for (int i = 0; i < nl && !st; ++i) {
+        ws = lane_ws[i];
+        stream = i ? lane_stream[i] : main;
+        st = embed_rows(first[i + 1] - first[i], rowmap + first[i], normalise);
+        normalised[i] = normalise;
     }
     {
         StepScope scope(in_step);
@@ -1438,12 +1470,13 @@ int Engine::decode_plan(int R, const std::vector<int>& lens, DecodePlan* dp) {
     return BST_OK;
 }
 
-int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens) {
+int Engine::decode_layers(int R, const int* rowmap, const std::vector<int>& lens,
+                          bool x_normalised) {
     // GEMMs enqueued below are profiled as the decode step's (kGemmStep).
     StepScope scope(in_step);
     DecodePlan dp;
     int st = decode_plan(R, lens, &dp);
-    bool x_normalised = false;  // ws.xs_* holds this layer's LN1 (or the final LN) of ws.x
+    // x_normalised: ws.xs_* holds this layer's LN1 (or the final LN) of ws.x
     for (int l = 0; l < L && !st; ++l) st = decode_layer(l, R, rowmap, dp, &x_normalised);
     return st ? st : decode_head(R, rowmap, x_normalised);
 }

@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "device.cuh"
@@ -856,7 +857,57 @@ __global__ __launch_bounds__(256) void k_splitk_reduce_logits_best(const float* 
     const size_t total = static_cast<size_t>(M) * N;
     unsigned long long best = 0ull;
     float* out = ea.out + static_cast<size_t>(ea.rowmap[m]) * ea.ldo;
-    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+    // Vector path: every thread loads all its columns' partials (16-byte loads, up to kCols
+    // columns and kMaxZ splits) before summing any, so the row costs one round trip to L2.
+    constexpr int kCols = 16, kMaxZ = 4;
+    const bool vec = splits <= kMaxZ && N <= kCols * static_cast<int>(blockDim.x) && (N % 4) == 0 &&
+                     (reinterpret_cast<uintptr_t>(part) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                     (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
+    if (vec) {
+        float4 t[kCols / 4][kMaxZ];
+#pragma unroll
+        for (int c = 0; c < kCols / 4; ++c) {
+            const int n = 4 * (threadIdx.x + c * blockDim.x);
+#pragma unroll
+            for (int z = 0; z < kMaxZ; ++z) {
+                t[c][z] = n < N && z < splits
+                              ? __ldcg(reinterpret_cast<const float4*>(part + z * total + m * static_cast<size_t>(N) + n))
+                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < kCols / 4; ++c) {
+            const int n = 4 * (threadIdx.x + c * blockDim.x);
+            if (n >= N) continue;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int z = 0; z < kMaxZ; ++z) {
+                if (z < splits) {
+                    v[0] += t[c][z].x;
+                    v[1] += t[c][z].y;
+                    v[2] += t[c][z].z;
+                    v[3] += t[c][z].w;
+                }
+            }
+            if (bias) {
+                const float4 b = *reinterpret_cast<const float4*>(bias + n);
+                v[0] = __fadd_rn(v[0], b.x);
+                v[1] = __fadd_rn(v[1], b.y);
+                v[2] = __fadd_rn(v[2], b.z);
+                v[3] = __fadd_rn(v[3], b.w);
+            }
+            *reinterpret_cast<float4*>(out + n) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (!isnan(v[j])) {
+                    const unsigned long long p = pack_best(v[j], n + j);
+                    best = p > best ? p : best;
+                }
+            }
+        }
+    }
+    for (int n = vec ? N : threadIdx.x; n < N; n += blockDim.x) {
         const size_t e = static_cast<size_t>(m) * N + n;
         float t[8];
 #pragma unroll
@@ -1109,19 +1160,23 @@ int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out) {
     // each split keeps at least four k-tiles (measured on the decode step against two, six and
     // eight: fewer partials to sum beats the shorter split GEMMs up to that point).
     const int tiles_m = (M + BM - 1) / BM;
-    const int bn = ((N + 127) / 128) * tiles_m >= 148 ? 128 : 64;
-    const int tiles = ((N + bn - 1) / bn) * tiles_m;
     const int k_tiles = (K + (w_bf16 ? 63 : 31)) / (w_bf16 ? 64 : 32);
-    int splits = 1;
-    if (tiles < 148) {
-        splits = std::min((148 + tiles - 1) / tiles, std::max(1, k_tiles / 4));
-        const size_t per_split = static_cast<size_t>(M) * N * sizeof(float);
-        while (splits > 1 && per_split * splits > part_bytes) --splits;
-        if (splits > 1) {
-            const int per = (k_tiles + splits - 1) / splits;
-            splits = (k_tiles + per - 1) / per;  // no empty split
+    auto plan = [&](int bn) {
+        const int tiles = ((N + bn - 1) / bn) * tiles_m;
+        int splits = 1;
+        if (tiles < 148) {
+            splits = std::min((148 + tiles - 1) / tiles, std::max(1, k_tiles / 4));
+            const size_t per_split = static_cast<size_t>(M) * N * sizeof(float);
+            while (splits > 1 && per_split * splits > part_bytes) --splits;
+            if (splits > 1) {
+                const int per = (k_tiles + splits - 1) / splits;
+                splits = (k_tiles + per - 1) / per;  // no empty split
+            }
         }
-    }
+        return splits;
+    };
+    int bn = ((N + 127) / 128) * tiles_m >= 148 ? 128 : 64;
+    int splits = plan(bn);
     if (bn_out) *bn_out = bn;
     return splits;
 }

@@ -360,6 +360,94 @@ __global__ void k_gather_last(const float* __restrict__ x, const int* __restrict
     for (int e = threadIdx.x; e < d; e += blockDim.x) last[static_cast<size_t>(j) * d + e] = x[src + e];
 }
 
+// Decode step begin fused with the first layer's LayerNorm: one CTA of 128 threads per row
+// embeds the row's next token at its slot (as k_embed_decode), then normalises the row with f64
+// statistics (as k_reduce_residual_ln, nn_ops.rs:168-199) straight into the QKV projection's
+// operand planes.
+template <typename WT, int EPT>
+__global__ __launch_bounds__(128) void k_embed_ln_decode(
+    const WT* __restrict__ tok, const WT* __restrict__ pos, const int* __restrict__ rowmap,
+    const int* __restrict__ next, int* __restrict__ len, int* __restrict__ slot,
+    float* __restrict__ x, int d, const float* __restrict__ gamma, const float* __restrict__ beta,
+    float eps, void* __restrict__ hi, void* __restrict__ lo, int planes) {
+    __shared__ double red[4];
+    __shared__ double stat;
+    __shared__ int s_slot, s_id;
+    const int i = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // LayerNorm parameters are weights: read before the wait.
+    float gv[EPT], tv[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        gv[j] = n < d ? gamma[n] : 0.0f;
+        tv[j] = n < d ? beta[n] : 0.0f;
+    }
+    pdl_trigger();
+    pdl_wait();
+    if (tid == 0) {
+        const int row = rowmap[i];
+        s_slot = len[row];
+        s_id = next[row];
+    }
+    __syncthreads();
+    const int sl = s_slot;
+    const size_t id = static_cast<size_t>(s_id);
+    float v[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        v[j] = n < d ? __fadd_rn(to_f(tok[id * d + n]), to_f(pos[static_cast<size_t>(sl) * d + n]))
+                     : 0.0f;
+        if (n < d) x[static_cast<size_t>(i) * d + n] = v[j];
+    }
+    if (tid == 0) {
+        slot[i] = sl;
+        len[rowmap[i]] = sl + 1;
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        if (tid + 128 * j < d) s = __dadd_rn(s, static_cast<double>(v[j]));
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (tid == 0) stat = __ddiv_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])),
+                                   static_cast<double>(d));
+    __syncthreads();
+    const double mean = stat;
+    double q = 0.0;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        if (tid + 128 * j < d) {
+            const double delta = __dadd_rn(static_cast<double>(v[j]), -mean);
+            q = __dadd_rn(q, __dmul_rn(delta, delta));
+        }
+    }
+    q = warp_sum_d(q);
+    __syncthreads();
+    if (lane == 0) red[warp] = q;
+    __syncthreads();
+    if (tid == 0) {
+        const double variance = __ddiv_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])),
+                                          static_cast<double>(d));
+        stat = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(variance, static_cast<double>(eps))));
+    }
+    __syncthreads();
+    const double inverse = stat;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+        const int n = tid + 128 * j;
+        if (n < d) {
+            const float normalized =
+                static_cast<float>(__dmul_rn(__dadd_rn(static_cast<double>(v[j]), -mean), inverse));
+            const float out = __fadd_rn(__fmul_rn(normalized, gv[j]), tv[j]);
+            store_split(out, planes, hi, lo, static_cast<size_t>(i) * d + n);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // LayerNorm (nn_ops.rs:168-199): one warp per row; mean and population variance in f64, the
 // normalised value rounded to f32, then f32 n * gamma + beta.
@@ -1219,6 +1307,28 @@ cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos
                                                     len, slot, x, d);
     }
     return err;
+}
+
+cudaError_t launch_embed_ln_decode(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
+                                   const int* rowmap, const int* next, int* len, int* slot, float* x,
+                                   int R, int d, const float* gamma, const float* beta, float eps,
+                                   void* hi, void* lo, int planes) {
+    if (R <= 0) return cudaSuccess;
+    if (d > 8 * 128 || planes < 1) return cudaErrorInvalidValue;
+#define BST_EMBED_LN(WT, EPT)                                                                      \
+    return launch_pdl(k_embed_ln_decode<WT, EPT>, R, 128, 0, s, static_cast<const WT*>(tok),       \
+                      static_cast<const WT*>(pos), rowmap, next, len, slot, x, d, gamma, beta, eps, \
+                      hi, lo, planes)
+    const int ept = (d + 127) / 128;
+    if (w_bf16) {
+        if (ept <= 2) BST_EMBED_LN(__nv_bfloat16, 2);
+        if (ept <= 4) BST_EMBED_LN(__nv_bfloat16, 4);
+        BST_EMBED_LN(__nv_bfloat16, 8);
+    }
+    if (ept <= 2) BST_EMBED_LN(float, 2);
+    if (ept <= 4) BST_EMBED_LN(float, 4);
+    BST_EMBED_LN(float, 8);
+#undef BST_EMBED_LN
 }
 
 cudaError_t launch_layernorm(cudaStream_t s, const float* x, int ldx, const float* gamma,

@@ -95,6 +95,14 @@ cudaError_t launch_embed_decode(cudaStream_t s, const void* tok, const void* pos
                                 const int* rowmap, const int* next, int* len, int* slot, float* x,
                                 int R, int d);
 
+// launch_embed_decode followed by the LayerNorm (gamma, beta, eps) of the embedded rows into
+// operand planes hi/lo ([R, d]; planes = 1 tf32, 2 bf16) for the first layer's QKV projection.
+// d <= 1024.
+cudaError_t launch_embed_ln_decode(cudaStream_t s, const void* tok, const void* pos, int w_bf16,
+                                   const int* rowmap, const int* next, int* len, int* slot, float* x,
+                                   int R, int d, const float* gamma, const float* beta, float eps,
+                                   void* hi, void* lo, int planes);
+
 // LayerNorm over the last dimension with f64 statistics (nn_ops.rs:168-199). Writes y (fp32,
 // optional) and, with planes = 1 (tf32) or 2 (bf16), the split operand planes hi/lo ([rows, d])
 // that the tensor-core GEMM consumes.
