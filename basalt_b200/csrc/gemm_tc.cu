@@ -23,7 +23,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 
 #include "device.cuh"
@@ -1177,6 +1176,13 @@ int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out) {
     };
     int bn = ((N + 127) / 128) * tiles_m >= 148 ? 128 : 64;
     int splits = plan(bn);
+    // A decode lane's GEMM (one 128-row tile) whose 64-wide plan takes more than half the SMs:
+    // 128-wide tiles halve its CTAs, so that the two decode lanes' GEMMs run in one wave (and
+    // each activation tile is read by half as many CTAs).
+    if (bn == 64 && tiles_m == 1 && N >= 128 && ((N + 63) / 64) * splits > 74) {
+        bn = 128;
+        splits = plan(bn);
+    }
     if (bn_out) *bn_out = bn;
     return splits;
 }
