@@ -1145,23 +1145,57 @@ __global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict_
         weights[i] = exp(__ddiv_rn(__dadd_rn(static_cast<double>(lr[order[i]]), -maximum), temperature));
     }
     __syncthreads();
+    // The total, summed in sorted order by one thread; each running sum overwrites its weight,
+    // so weights[i] becomes the reference loop's running sum after adding weight i. The weights
+    // are read eight at a time ahead of the additions (16-byte shared loads), so the loop runs
+    // at the latency of the f64 additions.
+    __shared__ double s_target;
+    __shared__ int s_first;
     if (threadIdx.x == 0) {
         double total = 0.0;
-        for (int i = 0; i < top_k; ++i) total = __dadd_rn(total, weights[i]);
+        int i = 0;
+        double2* w2 = reinterpret_cast<double2*>(weights);  // P is a power of two >= 8
+        for (; i + 8 <= top_k; i += 8) {
+            const double2 a = w2[i / 2], b = w2[i / 2 + 1], c = w2[i / 2 + 2], e = w2[i / 2 + 3];
+            double2 pa, pb, pc, pe;
+            total = __dadd_rn(total, a.x); pa.x = total;
+            total = __dadd_rn(total, a.y); pa.y = total;
+            total = __dadd_rn(total, b.x); pb.x = total;
+            total = __dadd_rn(total, b.y); pb.y = total;
+            total = __dadd_rn(total, c.x); pc.x = total;
+            total = __dadd_rn(total, c.y); pc.y = total;
+            total = __dadd_rn(total, e.x); pe.x = total;
+            total = __dadd_rn(total, e.y); pe.y = total;
+            w2[i / 2] = pa;
+            w2[i / 2 + 1] = pb;
+            w2[i / 2 + 2] = pc;
+            w2[i / 2 + 3] = pe;
+        }
+        for (; i < top_k; ++i) {
+            total = __dadd_rn(total, weights[i]);
+            weights[i] = total;
+        }
         uint64_t state = rng[r];
-        const double target = __dmul_rn(rng_next_double(state), total);
+        s_target = __dmul_rn(rng_next_double(state), total);
         rng[r] = state;
-        double running = 0.0;
-        int chosen = order[top_k - 1];
-        for (int i = 0; i < top_k; ++i) {
-            running = __dadd_rn(running, weights[i]);
-            if (target <= running) {
-                chosen = order[i];
+        s_first = top_k - 1;  // no running sum reaches the target: the last kept token
+    }
+    __syncthreads();
+    // The first i with target <= running sum i (TextEngine.java:420-425), found by every thread
+    // over its share of the running sums.
+    {
+        const double target = s_target;
+        int first = top_k;
+        for (int i = threadIdx.x; i < top_k; i += blockDim.x) {
+            if (target <= weights[i]) {
+                first = i;
                 break;
             }
         }
-        s_token = chosen;
+        if (first < top_k) atomicMin(&s_first, first);
     }
+    __syncthreads();
+    if (threadIdx.x == 0) s_token = order[s_first];
     __syncthreads();
     finish_row(r, s_token, s_step, rows, W, steps, step, done, tokens, next, window);
 }
