@@ -1102,11 +1102,86 @@ __device__ __forceinline__ uint64_t sort_key(float value, int index) {
     return (static_cast<uint64_t>(~ascending) << 32) | static_cast<uint32_t>(index);
 }
 
+// Threads of a sampling CTA: two CTAs share an SM (registers), so that one row's sequential sums
+// run beside another row's sort.
+constexpr int kSampleThreads = 512;
+
+// One compare-exchange pass (k, j) of an ascending bitonic sort of keys[0..P) in shared memory,
+// pairs spread over the block's threads.
+__device__ __forceinline__ void bitonic_pass_shared(uint64_t* keys, int P, int k, int j) {
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+            const uint64_t a = keys[i], b = keys[ixj];
+            if ((a > b) == ((i & k) == 0)) {
+                keys[i] = b;
+                keys[ixj] = a;
+            }
+        }
+    }
+}
+
+// The same ascending bitonic network over P = E * blockDim.x keys, with thread t holding keys
+// [E t, E t + E) in registers: the passes with j < E exchange inside a thread, those with
+// E <= j < 32 E between the lanes of a warp (shuffles), and only those with j >= 32 E go through
+// shared memory. Every pass compares and exchanges the same pairs as bitonic_pass_shared, so the
+// result is the same sorted array. keys holds the input on entry and the sorted keys on return.
+template <int E>
+__device__ __forceinline__ void bitonic_sort_blocked(uint64_t* keys, int P) {
+    const int t = threadIdx.x;
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = keys[E * t + e];
+    for (int k = 2; k <= P; k <<= 1) {
+        if ((k >> 1) >= 32 * E) {
+            __syncthreads();  // every thread has read the previous round's keys
+#pragma unroll
+            for (int e = 0; e < E; ++e) keys[E * t + e] = v[e];
+            __syncthreads();
+            for (int j = k >> 1; j >= 32 * E; j >>= 1) {
+                bitonic_pass_shared(keys, P, k, j);
+                __syncthreads();
+            }
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[e] = keys[E * t + e];
+        }
+        for (int j = min(k >> 1, 16 * E); j >= E; j >>= 1) {
+            const int tj = j / E;  // partner lane offset
+            const bool lower = (t & tj) == 0;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                const uint64_t o = __shfl_xor_sync(kFull, v[e], tj);
+                const bool up = ((E * t + e) & k) == 0;
+                v[e] = (lower == up) ? (v[e] < o ? v[e] : o) : (v[e] > o ? v[e] : o);
+            }
+        }
+#pragma unroll
+        for (int j = E / 2; j >= 1; j >>= 1) {
+            if (j < k) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    if ((e & j) == 0) {
+                        const uint64_t a = v[e], b = v[e | j];
+                        if ((a > b) == (((E * t + e) & k) == 0)) {
+                            v[e] = b;
+                            v[e | j] = a;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < E; ++e) keys[E * t + e] = v[e];
+    __syncthreads();
+}
+
 // TextEngine.draw (TextEngine.java:403-427): stable descending sort, w_i = exp((s_i - max) / T)
 // in double over the first topK, total summed in sorted order, target = nextDouble() * total,
 // first i with target <= running sum (else topK - 1). The sums run sequentially in one thread so
 // they round exactly as the reference's loop does.
-__global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict__ logits, int V,
+__global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float* __restrict__ logits, int V,
                                                         int P, int W, int steps, int rows,
                                                         double temperature, int top_k,
                                                         uint64_t* rng, int* step, int* done,
@@ -1122,19 +1197,18 @@ __global__ __launch_bounds__(1024) void k_select_sample(const float* __restrict_
     if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile int*>(step);
     for (int v = threadIdx.x; v < P; v += blockDim.x) keys[v] = v < V ? sort_key(lr[v], v) : ~0ULL;
     __syncthreads();
-    for (int k = 2; k <= P; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < P; i += blockDim.x) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const uint64_t a = keys[i], b = keys[ixj];
-                    if ((a > b) == ((i & k) == 0)) {
-                        keys[i] = b;
-                        keys[ixj] = a;
-                    }
-                }
+    if (P == 16 * static_cast<int>(blockDim.x)) {
+        bitonic_sort_blocked<16>(keys, P);
+    } else if (P == 8 * static_cast<int>(blockDim.x)) {
+        bitonic_sort_blocked<8>(keys, P);
+    } else if (P == 4 * static_cast<int>(blockDim.x)) {
+        bitonic_sort_blocked<4>(keys, P);
+    } else {
+        for (int k = 2; k <= P; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                bitonic_pass_shared(keys, P, k, j);
+                __syncthreads();
             }
-            __syncthreads();
         }
     }
     for (int i = threadIdx.x; i < top_k; i += blockDim.x) order[i] = static_cast<int>(keys[i] & 0xffffffffu);
@@ -1521,12 +1595,12 @@ cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, 
                                  int steps, float temperature, int top_k, uint64_t* rng,
                                  int* step, int* done, int* tokens, int* next, int* window) {
     if (rows <= 0) return cudaSuccess;
-    if (W > 8 * 1024) return cudaErrorInvalidValue;
+    if (W > 8 * kSampleThreads) return cudaErrorInvalidValue;
     int P = 1;
     while (P < V) P <<= 1;
     const size_t smem = select_sample_smem(V);
     if (smem > kSampleSmemLimit) return cudaErrorInvalidValue;
-    return launch_pdl(k_select_sample, rows, 1024, smem, s, logits, V, P, W, steps, rows,
+    return launch_pdl(k_select_sample, rows, kSampleThreads, smem, s, logits, V, P, W, steps, rows,
                                              static_cast<double>(temperature), top_k, rng, step,
                                              done, tokens, next, window);
 }
