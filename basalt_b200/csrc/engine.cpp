@@ -451,6 +451,11 @@ struct Workspace {
     float* history = nullptr;                 // per-step logits, when requested
     int* hist_rows_of = nullptr;              // history row h holds the logits of this wave row
     size_t hist_capacity = 0;                 // floats the history buffer holds
+    // Sampled runs over more rows than SMs: each row's sorted weights and token ids, handed from
+    // the sorting kernel to the warp-per-row draw ([rows][V]).
+    double* sorted_w = nullptr;
+    int* sorted_ids = nullptr;
+    size_t sorted_capacity = 0;               // rows x V entries
     void *xs_hi = nullptr, *xs_lo = nullptr;  // split operand planes of the tensor-core path
     void *ys_hi = nullptr, *ys_lo = nullptr;  // planes a producer writes for the next projection
     // The second decode lane's operand planes ([rows][max(d, F)]) and split-K partials.
@@ -643,7 +648,8 @@ class Engine {
     // ---- parameters ----
     int upload_weights();
     // hist_rows: rows whose per-step logits this run keeps (0: none).
-    int ensure_workspace(int rows, int steps, int slots, int tokens, int splits, int hist_rows);
+    int ensure_workspace(int rows, int steps, int slots, int tokens, int splits, int hist_rows,
+                         bool sampling);
     void free_workspace();
 
     // ---- runs ----
@@ -929,10 +935,13 @@ void Engine::free_workspace() {
 }
 
 int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int splits,
-                             int hist_rows) {
+                             int hist_rows, bool sampling) {
     const size_t hist_floats = static_cast<size_t>(hist_rows) * steps * V;
+    // The split draw pays off once the rows outnumber the SMs (one sorting CTA per row).
+    const size_t sorted = sampling && rows > 148 ? static_cast<size_t>(rows) * V : 0;
     if (ws.arena.ptr && ws.rows >= rows && ws.steps >= steps && ws.slots == slots &&
-        ws.tokens >= tokens && ws.splits >= splits && ws.hist_capacity >= hist_floats) {
+        ws.tokens >= tokens && ws.splits >= splits && ws.hist_capacity >= hist_floats &&
+        ws.sorted_capacity >= sorted) {
         return BST_OK;
     }
     free_workspace();
@@ -977,6 +986,10 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     }
     add(reinterpret_cast<void**>(&ws.rng), sizeof(uint64_t) * rows);
     add(reinterpret_cast<void**>(&ws.logits), sizeof(float) * static_cast<size_t>(rows) * V);
+    if (sorted) {
+        add(reinterpret_cast<void**>(&ws.sorted_w), sizeof(double) * sorted);
+        add(reinterpret_cast<void**>(&ws.sorted_ids), sizeof(int) * sorted);
+    }
     if (hist_floats) {
         add(reinterpret_cast<void**>(&ws.history), sizeof(float) * hist_floats);
         add(reinterpret_cast<void**>(&ws.hist_rows_of), sizeof(int) * rows);
@@ -1030,6 +1043,7 @@ int Engine::ensure_workspace(int rows, int steps, int slots, int tokens, int spl
     ws.tokens = tokens;
     ws.splits = splits;
     ws.hist_capacity = hist_floats;
+    ws.sorted_capacity = sorted;
     ws.generation = next_generation++;
     err = bst::launch_iota(stream, ws.rowmap_all, rows);
     if (!err && ws.attn_tickets) {
@@ -1727,9 +1741,11 @@ int Engine::enqueue_select(Mode mode, int rows, int steps, float temperature, in
         });
     } else {
         err = launch(bst::kSelectSample, rows * V * 4.0, 0, 1, [&] {
+            const bool split = ws.sorted_w && ws.sorted_capacity >= static_cast<size_t>(rows) * V;
             return bst::launch_select_sample(stream, ws.logits, rows, V, W, steps, temperature,
                                              top_k, ws.rng, ws.step, ws.done, ws.tokens_out,
-                                             ws.next, ws.window);
+                                             ws.next, ws.window, split ? ws.sorted_w : nullptr,
+                                             split ? ws.sorted_ids : nullptr);
         });
     }
     return err ? cuda_fail(err, "token selection") : BST_OK;
@@ -1776,7 +1792,8 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     const bool transformer = decoder_family(spec.family);
     if (transformer) plan(windows, rows, run_steps, &plans, &max_slots, &max_tokens);
     const int splits_cap = std::max(1, (max_slots + 31) / 32);
-    int st = ensure_workspace(rows, run_steps, max_slots, max_tokens, splits_cap, hist_rows);
+    int st = ensure_workspace(rows, run_steps, max_slots, max_tokens, splits_cap, hist_rows,
+                              mode == Mode::kSample);
     if (st) return st;
     hist_count = hist_rows;
 

@@ -1185,7 +1185,9 @@ __global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float
                                                         int P, int W, int steps, int rows,
                                                         double temperature, int top_k,
                                                         uint64_t* rng, int* step, int* done,
-                                                        int* tokens, int* next, int* window) {
+                                                        int* tokens, int* next, int* window,
+                                                        double* __restrict__ wout,
+                                                        int* __restrict__ oout) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) unsigned char smem[];
@@ -1219,6 +1221,15 @@ __global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float
         weights[i] = exp(__ddiv_rn(__dadd_rn(static_cast<double>(lr[order[i]]), -maximum), temperature));
     }
     __syncthreads();
+    if (wout) {
+        // The sums and the draw run in k_sample_draw, a warp per row: hand over the sorted
+        // weights and token ids.
+        for (int i = threadIdx.x; i < top_k; i += blockDim.x) {
+            wout[static_cast<size_t>(r) * V + i] = weights[i];
+            oout[static_cast<size_t>(r) * V + i] = order[i];
+        }
+        return;
+    }
     // The total, summed in sorted order by one thread; each running sum overwrites its weight,
     // so weights[i] becomes the reference loop's running sum after adding weight i. The weights
     // are read eight at a time ahead of the additions (16-byte shared loads), so the loop runs
@@ -1272,6 +1283,100 @@ __global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float
     if (threadIdx.x == 0) s_token = order[s_first];
     __syncthreads();
     finish_row(r, s_token, s_step, rows, W, steps, step, done, tokens, next, window);
+}
+
+// The rest of TextEngine.draw (TextEngine.java:416-427) for rows whose sorted weights and token
+// ids k_select_sample handed over (wts, ord: [rows][V], the first top_k of each row), one warp per
+// row, so that every row's sequential sums run at once. The whole warp walks the weights in
+// sorted order, lane j's weight broadcast to all lanes, each lane adding in the same order from
+// 0.0 (the reference's rounding); the running sum after every 32nd weight is kept (shared). The
+// target is nextDouble() * total; the drawn index is the first whose running sum reaches it: the
+// first 32-weight chunk whose last running sum does (running sums of non-negative weights never
+// decrease), then the same additions again inside that chunk from the previous chunk's sum.
+// Without a hit (NaN sums) the index is top_k - 1, as in the reference. Then the row's window
+// push and the step counter, as finish_row does.
+__global__ __launch_bounds__(256) void k_sample_draw(const double* __restrict__ wts,
+                                                     const int* __restrict__ ord, int V, int top_k,
+                                                     int W, int steps, int rows, uint64_t* rng,
+                                                     int* step, int* done, int* tokens, int* next,
+                                                     int* window) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ double s_ck[];  // [8 warps][chunks]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= rows) return;  // the whole warp
+    const int g = *reinterpret_cast<volatile int*>(step);
+    const double* w = wts + static_cast<size_t>(r) * V;
+    const int nch = (top_k + 31) / 32;
+    double* ck = s_ck + warp * nch;
+    double total = 0.0;
+    double cur = lane < top_k ? __ldcg(w + lane) : 0.0;
+    for (int c = 0; c < nch; ++c) {
+        const int base = c * 32;
+        const double nxt = base + 32 + lane < top_k ? __ldcg(w + base + 32 + lane) : 0.0;
+        const int n = min(32, top_k - base);
+        if (n == 32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) total = __dadd_rn(total, __shfl_sync(kFull, cur, j));
+        } else {
+            for (int j = 0; j < n; ++j) total = __dadd_rn(total, __shfl_sync(kFull, cur, j));
+        }
+        if (lane == 0) ck[c] = total;
+        cur = nxt;
+    }
+    double target = 0.0;
+    if (lane == 0) {
+        uint64_t state = rng[r];
+        target = __dmul_rn(rng_next_double(state), total);
+        rng[r] = state;
+    }
+    target = __shfl_sync(kFull, target, 0);
+    __syncwarp();
+    int first = nch;
+    for (int c = lane; c < nch; c += 32) {
+        if (target <= ck[c]) {
+            first = c;
+            break;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(kFull, first, o));
+    int chosen = top_k - 1;
+    if (first < nch) {
+        const int base = first * 32;
+        const int n = min(32, top_k - base);
+        double run = first > 0 ? ck[first - 1] : 0.0;
+        const double v = lane < n ? __ldcg(w + base + lane) : 0.0;
+        int hit = n;
+        for (int j = 0; j < n; ++j) {
+            run = __dadd_rn(run, __shfl_sync(kFull, v, j));
+            if (hit == n && target <= run) hit = j;
+        }
+        chosen = base + min(hit, n - 1);
+    }
+    const int token = __ldcg(ord + static_cast<size_t>(r) * V + chosen);
+    // TextEngine.push (TextEngine.java:387-390): shift the window left by one, in 32-wide
+    // chunks from the front (each chunk reads the positions after it before writing its own).
+    int* win = window + static_cast<size_t>(r) * W;
+    for (int base = 0; base < W; base += 32) {
+        const int t = base + lane;
+        const int carry = t + 1 < W ? win[t + 1] : token;
+        __syncwarp();
+        if (t < W) win[t] = carry;
+        __syncwarp();
+    }
+    if (lane == 0) {
+        tokens[static_cast<size_t>(r) * steps + g] = token;
+        next[r] = token;
+        __threadfence();
+        const int prev = atomicAdd(done, 1);
+        if (prev == rows - 1) {
+            *done = 0;
+            *step = g + 1;
+            __threadfence();
+        }
+    }
 }
 
 __global__ void k_stash_logits(const float* __restrict__ logits, int V, int steps,
@@ -1585,6 +1690,10 @@ cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, 
                                          window);
 }
 
+size_t sample_draw_smem(int top_k) {
+    return static_cast<size_t>(8) * ((top_k + 31) / 32) * sizeof(double);
+}
+
 size_t select_sample_smem(int V) {
     int P = 1;
     while (P < V) P <<= 1;
@@ -1593,16 +1702,23 @@ size_t select_sample_smem(int V) {
 
 cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, int V, int W,
                                  int steps, float temperature, int top_k, uint64_t* rng,
-                                 int* step, int* done, int* tokens, int* next, int* window) {
+                                 int* step, int* done, int* tokens, int* next, int* window,
+                                 double* sorted_w, int* sorted_ids) {
     if (rows <= 0) return cudaSuccess;
     if (W > 8 * kSampleThreads) return cudaErrorInvalidValue;
     int P = 1;
     while (P < V) P <<= 1;
     const size_t smem = select_sample_smem(V);
     if (smem > kSampleSmemLimit) return cudaErrorInvalidValue;
-    return launch_pdl(k_select_sample, rows, kSampleThreads, smem, s, logits, V, P, W, steps, rows,
-                                             static_cast<double>(temperature), top_k, rng, step,
-                                             done, tokens, next, window);
+    const size_t draw_smem = sample_draw_smem(top_k);
+    const bool split = sorted_w && sorted_ids && draw_smem <= 48 * 1024;
+    cudaError_t err = launch_pdl(k_select_sample, rows, kSampleThreads, smem, s, logits, V, P, W,
+                                 steps, rows, static_cast<double>(temperature), top_k, rng, step,
+                                 done, tokens, next, window, split ? sorted_w : nullptr,
+                                 split ? sorted_ids : nullptr);
+    if (err || !split) return err;
+    return launch_pdl(k_sample_draw, (rows + 7) / 8, 256, draw_smem, s, sorted_w, sorted_ids, V,
+                      top_k, W, steps, rows, rng, step, done, tokens, next, window);
 }
 
 namespace {

@@ -162,11 +162,15 @@ cudaError_t launch_last_token(cudaStream_t s, const int* window, int W, const fl
 cudaError_t launch_select_greedy(cudaStream_t s, const float* logits, int rows, int V, int W,
                                  int steps, int* step, int* done, int* tokens, int* next,
                                  int* window, unsigned long long* best = nullptr);
-// TextEngine.draw (TextEngine.java:403-427) per row with java.util.Random state rng[r].
+// TextEngine.draw (TextEngine.java:403-427) per row with java.util.Random state rng[r]. With
+// sorted_w / sorted_ids ([rows][V] scratch) the sums and the draw run in a second kernel, one
+// warp per row, so that all rows' sequential sums run at once; without, one CTA does a row.
 cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, int V, int W,
                                  int steps, float temperature, int top_k, uint64_t* rng,
-                                 int* step, int* done, int* tokens, int* next, int* window);
+                                 int* step, int* done, int* tokens, int* next, int* window,
+                                 double* sorted_w = nullptr, int* sorted_ids = nullptr);
 size_t select_sample_smem(int V);
+size_t sample_draw_smem(int top_k);
 
 // Sets kernel attributes that must be in place before the first launch on the current device.
 cudaError_t configure_device_kernels();
