@@ -694,6 +694,13 @@ class Engine {
     // layer's LayerNorm of them into the operand planes ws.xs_*).
     int embed_rows(int R, const int* rowmap, bool normalise);
     int decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp, bool* x_normalised);
+    // Layer l after its QKV projection: attention over the cache for R rows (q in ws.q, or summed
+    // from the projection's split-K partials), output projection, LN2, FFN, and the next LN.
+    // attn_class: the profiling class of its attention launch (the prefill's last layer counts
+    // as prefill attention).
+    int decode_after_qkv(int l, int R, const int* rowmap, const DecodePlan& dp,
+                         const bst::QkvParts& qparts, bool* x_normalised,
+                         int attn_class = bst::kAttnDecode);
     int decode_head(int R, const int* rowmap, bool x_normalised);
     int qkv_partials(const LayerWeights& lw, const bst::LnArgs* ln, int R, int splits);
     int enqueue_direct(int rows);
@@ -1289,6 +1296,43 @@ int Engine::enqueue_prefill(const StepPlan& p, size_t begin, size_t end) {
         qkv.kv_bf16 = kvbf16;
         st = linear(ws.x, d, lw.wqkv, lw.bqkv, T, 3 * d, d, Epi::kQkv, qkv, "qkv projection", &ln1);
         if (st) return st;
+        if (l == L - 1 && T > segs) {
+            // Only each segment's last position feeds the head, and the cache now holds every
+            // key and value of the segment: the rest of the last layer runs as a decode step
+            // over the segments' last queries and residual rows (attention over the row's
+            // cached keys [0, len) is the causal attention of its last position).
+            err = bst::launch_gather_last(stream, ws.q, ws.seg_start, ws.seg_len, segs, d,
+                                          ws.last_h);
+            if (!err) {
+                err = bst::launch_gather_last(stream, ws.x, ws.seg_start, ws.seg_len, segs, d,
+                                              ws.last);
+            }
+            if (err) return cuda_fail(err, "gather last");
+            const Workspace saved = ws;
+            ws.x = ws.last;
+            ws.q = ws.last_h;
+            DecodePlan dp;
+            bool normalised = false;
+            st = decode_plan(segs, std::vector<int>(p.prefill_len.begin() + begin,
+                                                    p.prefill_len.begin() + end), &dp);
+            if (!st) {
+                st = decode_after_qkv(l, segs, ws.seg_row, dp, bst::QkvParts{}, &normalised,
+                                      bst::kAttnPrefill);
+            }
+            ws = saved;
+            if (st) return st;
+            EpiArgs lg;
+            lg.out = ws.logits;
+            lg.ldo = V;
+            lg.rowmap = ws.seg_row;
+            lg.best = head_argmax ? ws.best : nullptr;
+            if (normalised) {
+                return linear(ws.last, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head",
+                              nullptr, false, true);
+            }
+            const bst::LnArgs lnf{lnf_g, lnf_b, kLayerNormEps};
+            return linear(ws.last, d, head_w, head_b, segs, V, d, Epi::kLogits, lg, "head", &lnf);
+        }
         const bst::PlaneOut att_planes = planes_for(lw.wo, T, d, d);
         st = check(launch(bst::kAttnPrefill, attn_bytes, attn_flops, 1, [&] {
                        return bst::launch_attn_prefill(stream, ws.q, qkv.k_cache, qkv.v_cache,
@@ -1499,8 +1543,6 @@ int Engine::decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp,
                          bool* x_normalised) {
     const double kvb = kvbf16 ? 2.0 : 4.0;
     const int slots = ws.slots;
-    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
-    auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
     int st = BST_OK;
     const LayerWeights& lw = layers[l];
     const bst::LnArgs ln1{lw.ln1_g, lw.ln1_b, kLayerNormEps};
@@ -1532,6 +1574,21 @@ int Engine::decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp,
                                     "qkv projection", &ln1);
     }
     if (st) return st;
+    return decode_after_qkv(l, R, rowmap, dp, qparts, x_normalised);
+}
+
+int Engine::decode_after_qkv(int l, int R, const int* rowmap, const DecodePlan& dp,
+                             const bst::QkvParts& qparts, bool* x_normalised, int attn_class) {
+    const double kvb = kvbf16 ? 2.0 : 4.0;
+    const int slots = ws.slots;
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
+    auto check = [&](cudaError_t e, const char* what) { return e ? cuda_fail(e, what) : BST_OK; };
+    int st = BST_OK;
+    const LayerWeights& lw = layers[l];
+    void* const k_cache =
+        static_cast<char*>(ws.k_cache) + l * ws.kv_layer_elems * static_cast<size_t>(kvb);
+    void* const v_cache =
+        static_cast<char*>(ws.v_cache) + l * ws.kv_layer_elems * static_cast<size_t>(kvb);
     const double kv_bytes = dp.sum_len * 2.0 * d * kvb + R * d * 4.0 +
                             (qparts.part ? qparts.splits * R * 3.0 * d * 4.0 : 0.0);
     const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
@@ -1539,8 +1596,8 @@ int Engine::decode_layer(int l, int R, const int* rowmap, const DecodePlan& dp,
         st = check(cudaStreamWaitEvent(stream, attn_after, 0), "ordering the lanes' attention");
         if (st) return st;
     }
-    st = check(launch(bst::kAttnDecode, kv_bytes, 4.0 * dp.sum_len * d, 1, [&] {
-                   return bst::launch_attn_decode(stream, ws.q, qkv.k_cache, qkv.v_cache,
+    st = check(launch(attn_class, kv_bytes, 4.0 * dp.sum_len * d, 1, [&] {
+                   return bst::launch_attn_decode(stream, ws.q, k_cache, v_cache,
                                                   kvbf16, rowmap, ws.len, R, H, hd, slots,
                                                   scale, dp.splits, dp.chunk, ws.part,
                                                   ws.attn_tickets,
