@@ -537,6 +537,23 @@ class Engine {
 
     bool profiling = false;
     bool in_step = false;  // enqueuing a batched decode step (decode_layers)
+    // Greedy steps whose head runs with a K split: the head's fix-up kernel pushes each row's
+    // token itself (decode_head sets it up, enqueue_select then has nothing left to do).
+    bool push_in_head = false;
+    bool push_allowed = false;  // this step decodes every row of the run (no prefill rows)
+    int push_steps = 0, push_rows = 0;
+    // Whether every decode lane's head (rows per lane in `lanes`) runs the split-K fix-up that
+    // can push the tokens.
+    bool head_pushes(const int* lanes, int n) const {
+        if (!push_allowed || !head_argmax || hist_count != 0 || W > 8 * 256) return false;
+        for (int i = 0; i < n; ++i) {
+            if (!linear_on_tc(head_w, lanes[i], V, d) ||
+                bst::tc_plan(lanes[i], V, d, wbf16, bst::tc_part_bytes_max(), nullptr) <= 1) {
+                return false;
+            }
+        }
+        return true;
+    }
     struct StepScope {
         bool& flag;
         explicit StepScope(bool& f) : flag(f) { flag = true; }
@@ -1404,6 +1421,12 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
                       !linear_on_tc(layers[0].wqkv, R / nl, 3 * d, d))) {
         nl /= 2;
     }
+    {
+        int lanes[kLanes];
+        for (int i = 0; i < nl; ++i) lanes[i] = (i + 1) * R / nl - i * R / nl;
+        push_in_head = head_pushes(lanes, nl);
+        push_rows = R;
+    }
     if (nl == 1) {
         // On the tensor-core path the embedding kernel also writes the first LayerNorm's
         // operand planes; the GEMV path normalises inside its own projection.
@@ -1637,6 +1660,16 @@ int Engine::decode_head(int R, const int* rowmap, bool x_normalised) {
     lg.ldo = V;
     lg.rowmap = rowmap;
     lg.best = head_argmax ? ws.best : nullptr;
+    if (push_in_head) {
+        lg.step = ws.step;
+        lg.done = ws.done;
+        lg.tokens = ws.tokens_out;
+        lg.next = ws.next;
+        lg.window = ws.window;
+        lg.window_len = W;
+        lg.steps = push_steps;
+        lg.rows = push_rows;
+    }
     return x_normalised ? linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head",
                                  nullptr, false, true)
                         : linear(ws.x, d, head_w, head_b, R, V, d, Epi::kLogits, lg, "head", &lnf);
@@ -1790,6 +1823,11 @@ int Engine::enqueue_select(Mode mode, int rows, int steps, float temperature, in
         });
         if (err) return cuda_fail(err, "stashing logits");
     }
+    if (mode == Mode::kGreedy && push_in_head) {
+        push_in_head = false;  // the head's fix-up pushed the tokens
+        return BST_OK;
+    }
+    push_in_head = false;
     if (mode == Mode::kGreedy) {
         err = launch(bst::kSelectGreedy, rows * V * 4.0, 0, 1, [&] {
             return bst::launch_select_greedy(stream, ws.logits, rows, V, W, steps, ws.step, ws.done,
@@ -1853,6 +1891,8 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
                               mode == Mode::kSample);
     if (st) return st;
     hist_count = hist_rows;
+    push_steps = run_steps;
+    push_in_head = false;
 
     cudaError_t err = cudaMemcpyAsync(ws.window, windows.data(), sizeof(int32_t) * windows.size(),
                                       cudaMemcpyHostToDevice, stream);
@@ -1895,6 +1935,7 @@ int Engine::run_wave(Mode mode, const std::vector<int32_t>& all_windows, int row
     std::vector<int32_t> step_tokens(rows);
     for (int g = 0; g < run_steps; ++g) {
         const bool all_decode = transformer && plans[g].prefill_rows.empty();
+        push_allowed = all_decode && static_cast<int>(plans[g].decode_rows.size()) == rows;
         const bool graphable = !profiling && mode != Mode::kScores &&
                                (transformer ? all_decode : true);
         if (transformer && !plans[g].prefill_rows.empty()) {

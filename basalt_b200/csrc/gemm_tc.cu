@@ -28,6 +28,7 @@
 #include "device.cuh"
 #include "epilogue.cuh"
 #include "kernels.h"
+#include "select.cuh"
 
 namespace bst {
 namespace {
@@ -852,7 +853,10 @@ __global__ __launch_bounds__(256) void k_splitk_reduce_logits_best(const float* 
     pdl_trigger();
     pdl_wait();
     __shared__ unsigned long long s_best[8];
+    __shared__ float s_first;
+    __shared__ int s_step, s_token;
     const int m = blockIdx.x;
+    if (ea.step && threadIdx.x == 0) s_step = *reinterpret_cast<volatile int*>(ea.step);
     const size_t total = static_cast<size_t>(M) * N;
     unsigned long long best = 0ull;
     float* out = ea.out + static_cast<size_t>(ea.rowmap[m]) * ea.ldo;
@@ -897,6 +901,7 @@ __global__ __launch_bounds__(256) void k_splitk_reduce_logits_best(const float* 
                 v[3] = __fadd_rn(v[3], b.w);
             }
             *reinterpret_cast<float4*>(out + n) = make_float4(v[0], v[1], v[2], v[3]);
+            if (n == 0) s_first = v[0];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 if (!isnan(v[j])) {
@@ -919,6 +924,7 @@ __global__ __launch_bounds__(256) void k_splitk_reduce_logits_best(const float* 
         for (int z = 8; z < splits; ++z) v += part[static_cast<size_t>(z) * total + e];
         if (bias) v = __fadd_rn(v, bias[n]);
         out[n] = v;
+        if (n == 0) s_first = v;
         if (!isnan(v)) {
             const unsigned long long p = pack_best(v, n);
             best = p > best ? p : best;
@@ -933,7 +939,18 @@ __global__ __launch_bounds__(256) void k_splitk_reduce_logits_best(const float* 
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = s_best[w] > best ? s_best[w] : best;
-        ea.best[ea.rowmap[m]] = best;
+        if (ea.step) {
+            // TextEngine.argmax (TextEngine.java:392-400): the first maximum; a NaN first
+            // score is never replaced, so it selects token 0.
+            s_token = (isnan(s_first) || best == 0ull) ? 0 : unpack_best_index(best);
+        } else {
+            ea.best[ea.rowmap[m]] = best;
+        }
+    }
+    if (ea.step) {
+        __syncthreads();
+        finish_row(ea.rowmap[m], s_token, s_step, ea.rows, ea.window_len, ea.steps, ea.step,
+                   ea.done, ea.tokens, ea.next, ea.window);
     }
 }
 
@@ -1182,6 +1199,13 @@ int tc_plan(int M, int N, int K, int w_bf16, size_t part_bytes, int* bn_out) {
     if (bn == 64 && tiles_m == 1 && N >= 128 && ((N + 63) / 64) * splits > 74) {
         bn = 128;
         splits = plan(bn);
+        // ... and with fewer splits where even the 128-wide plan takes more than half the SMs
+        // (the head of the V4096 model: 32 tiles x 4 splits -> x 2).
+        const int tiles128 = (N + 127) / 128;
+        while (splits > 1 && tiles128 * splits > 74) {
+            const int per = (k_tiles + splits - 2) / (splits - 1);
+            splits = (k_tiles + per - 1) / per;
+        }
     }
     if (bn_out) *bn_out = bn;
     return splits;

@@ -67,6 +67,16 @@ struct EpiArgs {
     // kLogits: per destination row, the packed first maximum of the row's logits (pack_best),
     // combined with 64-bit atomicMax; nullptr when the caller selects from the logits itself.
     unsigned long long* best = nullptr;
+    // kLogits with best and a K split: when step is set, the split-K fix-up (one block per row)
+    // also takes TextEngine.argmax's token from the row's maximum and pushes it, as
+    // k_select_greedy_packed does (window [rows][window_len], tokens [rows][steps], next, and
+    // the step counter advanced once all `rows` rows of the step are done).
+    int* step = nullptr;
+    int* done = nullptr;
+    int* tokens = nullptr;
+    int* next = nullptr;
+    int* window = nullptr;
+    int window_len = 0, steps = 0, rows = 0;
 };
 
 // Optional LayerNorm applied to a projection's input rows (the pre-norm of TransformerBlock).
