@@ -559,13 +559,6 @@ class Engine {
         explicit StepScope(bool& f) : flag(f) { flag = true; }
         ~StepScope() { flag = false; }
     };
-    // Lane ring of the batched decode step: with several lanes, each lane's attention kernel
-    // waits for the previous attention in the ring (lane i after lane i - 1 of the same layer,
-    // lane 0 after the last lane of the layer before), so the lanes take turns at streaming the
-    // cache while the others run their projections. decode_layer waits for attn_after (when
-    // set) before its attention and records attn_done after it.
-    cudaEvent_t lane_attn[kLanes] = {};
-    cudaEvent_t attn_after = nullptr, attn_done = nullptr;
     KernelStats stats[bst::kKernelClassCount];
     std::vector<PendingTiming> pending;
     std::vector<cudaEvent_t> event_pool;
@@ -612,10 +605,6 @@ class Engine {
         }
         if (lane_fork) cudaEventDestroy(lane_fork);
         lane_fork = nullptr;
-        for (int i = 0; i < kLanes; ++i) {
-            if (lane_attn[i]) cudaEventDestroy(lane_attn[i]);
-            lane_attn[i] = nullptr;
-        }
     }
 
     // ---- launches with optional per-class timing ----
@@ -1436,10 +1425,8 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
     }
     // Lane i takes rows [i R / nl, (i + 1) R / nl) with every per-row workspace view shifted to
     // them; lanes > 0 run on their own streams with private planes and partials. The lanes are
-    // enqueued layer by layer, so that BST_LANE_RING=1 in the environment can chain their
-    // attention kernels into a ring (see lane_attn).
-    const char* ring_env = std::getenv("BST_LANE_RING");
-    const bool ring = ring_env && std::atoi(ring_env) != 0;
+    // enqueued layer by layer and start together (chaining their attention kernels so that one
+    // lane streams the cache while the other runs its projections measured slower).
     cudaError_t err = cudaEventRecord(lane_fork, stream);
     for (int i = 1; i < nl && !err; ++i) err = cudaStreamWaitEvent(lane_stream[i], lane_fork, 0);
     if (err) return cuda_fail(err, "forking the decode lanes");
@@ -1485,13 +1472,10 @@ int Engine::enqueue_decode(int R, const int* rowmap, const std::vector<int>& len
             for (int i = 0; i < nl && !st; ++i) {
                 ws = lane_ws[i];
                 stream = i ? lane_stream[i] : main;
-                attn_after = ring && (l > 0 || i > 0) ? lane_attn[(i + nl - 1) % nl] : nullptr;
-                attn_done = ring ? lane_attn[i] : nullptr;
                 st = decode_layer(l, first[i + 1] - first[i], rowmap + first[i], plan[i],
                                   &normalised[i]);
             }
         }
-        attn_after = attn_done = nullptr;
         for (int i = 0; i < nl && !st; ++i) {
             ws = lane_ws[i];
             stream = i ? lane_stream[i] : main;
@@ -1615,10 +1599,6 @@ int Engine::decode_after_qkv(int l, int R, const int* rowmap, const DecodePlan& 
     const double kv_bytes = dp.sum_len * 2.0 * d * kvb + R * d * 4.0 +
                             (qparts.part ? qparts.splits * R * 3.0 * d * 4.0 : 0.0);
     const bst::PlaneOut att_planes = planes_for(lw.wo, R, d, d);
-    if (attn_after) {
-        st = check(cudaStreamWaitEvent(stream, attn_after, 0), "ordering the lanes' attention");
-        if (st) return st;
-    }
     st = check(launch(attn_class, kv_bytes, 4.0 * dp.sum_len * d, 1, [&] {
                    return bst::launch_attn_decode(stream, ws.q, k_cache, v_cache,
                                                   kvbf16, rowmap, ws.len, R, H, hd, slots,
@@ -1628,10 +1608,6 @@ int Engine::decode_after_qkv(int l, int R, const int* rowmap, const DecodePlan& 
                                                   att_planes, qparts);
                }), "decode attention");
     if (st) return st;
-    if (attn_done) {
-        st = check(cudaEventRecord(attn_done, stream), "ordering the lanes' attention");
-        if (st) return st;
-    }
     const bst::LnArgs ln2{lw.ln2_g, lw.ln2_b, kLayerNormEps};
     bool ffn_in_normalised = false;
     st = residual_ln(ws.att, d, lw.wo, lw.bo, R, d, d, att_planes.planes != 0, ln2,
@@ -2251,9 +2227,6 @@ int32_t bst_engine_create(const bst_model_spec* spec, int32_t device, bst_engine
             if (!err) err = cudaEventCreateWithFlags(&e->lane_join[i], cudaEventDisableTiming);
         }
         if (!err) err = cudaEventCreateWithFlags(&e->lane_fork, cudaEventDisableTiming);
-        for (int i = 0; i < kLanes && !err; ++i) {
-            err = cudaEventCreateWithFlags(&e->lane_attn[i], cudaEventDisableTiming);
-        }
         if (!err) err = bst::configure_device_kernels_once(device);
         if (err) {
             cudaGetLastError();
