@@ -486,16 +486,16 @@ __global__ __launch_bounds__(256) void k_layernorm(const float* __restrict__ x, 
 
 // Split-K fix-up of a residual projection, then the LayerNorm of the updated rows into operand
 // planes (see launch_reduce_residual_ln). One CTA of 128 threads per row; a thread owns EPT
-// columns (n = tid + 128 j) and loads their partials of up to 16 splits at once, together with
+// columns (n = tid + 128 j) and loads their partials of up to ZB splits at once, together with
 // the residual row (bias, gamma and beta are read before the PDL wait). The splits are summed in
 // order as k_splitk_reduce does; the f64 statistics are k_layernorm's up to the order of the f64
-// additions.
-template <int EPT>
+// additions. ZB is the launch's split count rounded up (4, 8 or 16), so that the registers
+// holding loads in flight stay few enough for several CTAs per SM.
+template <int EPT, int ZB>
 __global__ __launch_bounds__(128) void k_reduce_residual_ln(
     const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
     float* __restrict__ x, int ldx, const float* __restrict__ gamma, const float* __restrict__ beta,
     float eps, void* __restrict__ hi, void* __restrict__ lo, int planes) {
-    constexpr int ZB = 16;
     __shared__ double red[4];
     __shared__ double stat;
     const int m = blockIdx.x;
@@ -1579,12 +1579,18 @@ cudaError_t launch_reduce_residual_ln(cudaStream_t s, const float* part, int spl
                                       const float* bias, float* x, int ldx, const LnArgs& ln,
                                       void* hi, void* lo, int planes) {
     if (M <= 0) return cudaSuccess;
-#define BST_RRL(EPT)                                                                             \
-    return launch_pdl(k_reduce_residual_ln<EPT>, dim3(M), 128, 0, s, part, splits, M, N, bias, x, \
-                      ldx, ln.gamma, ln.beta, ln.eps, hi, lo, planes)
-    if (N <= 256) BST_RRL(2);
-    if (N <= 512) BST_RRL(4);
-    if (N <= 1024) BST_RRL(8);
+#define BST_RRL(EPT, ZB)                                                                         \
+    return launch_pdl(k_reduce_residual_ln<EPT, ZB>, dim3(M), 128, 0, s, part, splits, M, N, bias, \
+                      x, ldx, ln.gamma, ln.beta, ln.eps, hi, lo, planes)
+#define BST_RRL_Z(EPT)                    \
+    if (splits <= 4) BST_RRL(EPT, 4);     \
+    if (splits <= 8) BST_RRL(EPT, 8);     \
+    BST_RRL(EPT, 16)
+    if (N <= 256) { BST_RRL_Z(2); }
+    if (N <= 512) { BST_RRL_Z(4); }
+    if (N <= 768) { BST_RRL_Z(6); }
+    if (N <= 1024) { BST_RRL_Z(8); }
+#undef BST_RRL_Z
 #undef BST_RRL
     return cudaErrorInvalidValue;
 }
