@@ -356,12 +356,14 @@ __device__ __forceinline__ void publish_stats(const float* xown, int own_ld, int
     }
 }
 
-// Mean and 1/sqrt(var + eps) of R rows of width d from the published per-CTA statistics; warp i
-// handles row i. Results in mean[i], inv[i] (shared) after the caller's __syncthreads().
+// Mean and 1/sqrt(var + eps) of R rows of width d from the published per-CTA statistics; the
+// last R warps handle a row each (warp kWarps - R + i row i), so that their loads overlap the
+// row staging that the first threads of the CTA do. Results in mean[i], inv[i] (shared) after
+// the caller's __syncthreads().
 __device__ __forceinline__ void combine_stats(const double* stats, int R, int d, float eps,
                                               double* mean, double* inv) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp >= R) return;
+    const int warp = (threadIdx.x >> 5) - (kWarps - R), lane = threadIdx.x & 31;
+    if (warp < 0) return;
     const int G = gridDim.x;
     const int cpc = (d + G - 1) / G;
     const double* rs = stats + static_cast<size_t>(warp) * G * 2;
