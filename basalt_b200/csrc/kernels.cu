@@ -1177,6 +1177,92 @@ __device__ __forceinline__ void bitonic_sort_blocked(uint64_t* keys, int P) {
     __syncthreads();
 }
 
+// Stable LSD radix sort of P = E * blockDim.x 64-bit keys, ascending by their high 32 bits, in
+// eight passes of 4-bit digits; keys with equal high words keep their input order. With the sort
+// keys of sort_key (ordered score in the high word, index in the low word, entered in index
+// order) this is the same order as sorting the whole 64-bit keys. Per pass each thread holds E
+// consecutive keys, counts their digits in its own column of cnt ([16][blockDim.x] 16-bit
+// counters), an exclusive scan over cnt in digit-major order gives each (digit, thread) the
+// number of keys that precede its keys in the output, and every key goes straight to its place.
+__device__ __forceinline__ void scan_counts(uint16_t* cnt) {
+    // Exclusive prefix sum over cnt[0 .. 16 * blockDim.x): thread t owns entries [16 t, 16 t + 16).
+    __shared__ unsigned s_warp[32];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    uint4* c4 = reinterpret_cast<uint4*>(cnt) + 2 * t;
+    const uint4 a = c4[0], b = c4[1];
+    const unsigned w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    unsigned total = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) total += (w[i] & 0xffffu) + (w[i] >> 16);
+    unsigned incl = total;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        unsigned x = lane < nw ? s_warp[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(kFull, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane < nw) s_warp[lane] = x;
+    }
+    __syncthreads();
+    unsigned run = incl - total + (warp > 0 ? s_warp[warp - 1] : 0u);
+    unsigned out[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const unsigned lo = run;
+        run += w[i] & 0xffffu;
+        const unsigned hi = run;
+        run += w[i] >> 16;
+        out[i] = (lo & 0xffffu) | (hi << 16);
+    }
+    c4[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    c4[1] = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+template <int E>
+__device__ __forceinline__ void radix_sort_hi32(uint64_t* keys, uint16_t* cnt) {
+    const int t = threadIdx.x, B = blockDim.x;
+#pragma unroll 1
+    for (int pass = 0; pass < 8; ++pass) {
+        const int shift = 32 + 4 * pass;
+        uint64_t v[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = keys[E * t + e];
+#pragma unroll
+        for (int dg = 0; dg < 16; ++dg) cnt[dg * B + t] = 0;
+        unsigned lr[E / 2];  // each key's rank among the thread's earlier keys of its digit, two per word
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const int dg = static_cast<int>(v[e] >> shift) & 15;
+            const unsigned c = cnt[dg * B + t];
+            cnt[dg * B + t] = static_cast<uint16_t>(c + 1);
+            if (e & 1) {
+                lr[e / 2] |= c << 16;
+            } else {
+                lr[e / 2] = c;
+            }
+        }
+        __syncthreads();
+        scan_counts(cnt);
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const int dg = static_cast<int>(v[e] >> shift) & 15;
+            const unsigned rank = (e & 1) ? lr[e / 2] >> 16 : lr[e / 2] & 0xffffu;
+            keys[cnt[dg * B + t] + rank] = v[e];
+        }
+        __syncthreads();
+    }
+}
+
 // TextEngine.draw (TextEngine.java:403-427): stable descending sort, w_i = exp((s_i - max) / T)
 // in double over the first topK, total summed in sorted order, target = nextDouble() * total,
 // first i with target <= running sum (else topK - 1). The sums run sequentially in one thread so
@@ -1200,7 +1286,8 @@ __global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float
     for (int v = threadIdx.x; v < P; v += blockDim.x) keys[v] = v < V ? sort_key(lr[v], v) : ~0ULL;
     __syncthreads();
     if (P == 16 * static_cast<int>(blockDim.x)) {
-        bitonic_sort_blocked<16>(keys, P);
+        // 16 x blockDim.x 16-bit counters in the token-order array, written only after the sort
+        radix_sort_hi32<16>(keys, reinterpret_cast<uint16_t*>(order));
     } else if (P == 8 * static_cast<int>(blockDim.x)) {
         bitonic_sort_blocked<8>(keys, P);
     } else if (P == 4 * static_cast<int>(blockDim.x)) {
