@@ -1227,15 +1227,17 @@ __device__ __forceinline__ void scan_counts(uint16_t* cnt) {
     c4[1] = make_uint4(out[4], out[5], out[6], out[7]);
 }
 
+// keys holds key p at p + p / 16 (E must be 16).
 template <int E>
 __device__ __forceinline__ void radix_sort_hi32(uint64_t* keys, uint16_t* cnt) {
+    static_assert(E == 16, "the gap layout assumes 16 keys per thread");
     const int t = threadIdx.x, B = blockDim.x;
 #pragma unroll 1
     for (int pass = 0; pass < 8; ++pass) {
         const int shift = 32 + 4 * pass;
         uint64_t v[E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) v[e] = keys[E * t + e];
+        for (int e = 0; e < E; ++e) v[e] = keys[(E + 1) * t + e];  // key E t + e, with its gap
 #pragma unroll
         for (int dg = 0; dg < 16; ++dg) cnt[dg * B + t] = 0;
         unsigned lr[E / 2];  // each key's rank among the thread's earlier keys of its digit, two per word
@@ -1257,7 +1259,8 @@ __device__ __forceinline__ void radix_sort_hi32(uint64_t* keys, uint16_t* cnt) {
         for (int e = 0; e < E; ++e) {
             const int dg = static_cast<int>(v[e] >> shift) & 15;
             const unsigned rank = (e & 1) ? lr[e / 2] >> 16 : lr[e / 2] & 0xffffu;
-            keys[cnt[dg * B + t] + rank] = v[e];
+            const unsigned pos = cnt[dg * B + t] + rank;
+            keys[pos + (pos >> 4)] = v[e];
         }
         __syncthreads();
     }
@@ -1278,14 +1281,20 @@ __global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float
     pdl_wait();
     extern __shared__ __align__(16) unsigned char smem[];
     uint64_t* keys = reinterpret_cast<uint64_t*>(smem);
-    int* order = reinterpret_cast<int*>(keys + P);
+    // The radix path keeps key p at p + p / 16 (one gap per 16 keys), so that the 16 consecutive
+    // keys each thread loads fall in different banks across a warp; the array has room for the
+    // gaps, the token-order array follows it.
+    const bool radix = P == 16 * static_cast<int>(blockDim.x);
+    int* order = reinterpret_cast<int*>(keys + P + P / 16);
     const int r = blockIdx.x;
     const float* lr = logits + static_cast<size_t>(r) * V;
     __shared__ int s_step, s_token;
     if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile int*>(step);
-    for (int v = threadIdx.x; v < P; v += blockDim.x) keys[v] = v < V ? sort_key(lr[v], v) : ~0ULL;
+    for (int v = threadIdx.x; v < P; v += blockDim.x) {
+        keys[radix ? v + (v >> 4) : v] = v < V ? sort_key(lr[v], v) : ~0ULL;
+    }
     __syncthreads();
-    if (P == 16 * static_cast<int>(blockDim.x)) {
+    if (radix) {
         // 16 x blockDim.x 16-bit counters in the token-order array, written only after the sort
         radix_sort_hi32<16>(keys, reinterpret_cast<uint16_t*>(order));
     } else if (P == 8 * static_cast<int>(blockDim.x)) {
@@ -1300,7 +1309,9 @@ __global__ __launch_bounds__(kSampleThreads, 2) void k_select_sample(const float
             }
         }
     }
-    for (int i = threadIdx.x; i < top_k; i += blockDim.x) order[i] = static_cast<int>(keys[i] & 0xffffffffu);
+    for (int i = threadIdx.x; i < top_k; i += blockDim.x) {
+        order[i] = static_cast<int>(keys[radix ? i + (i >> 4) : i] & 0xffffffffu);
+    }
     __syncthreads();
     double* weights = reinterpret_cast<double*>(keys);  // reuse: keys are no longer needed
     const double maximum = static_cast<double>(lr[order[0]]);
@@ -1790,7 +1801,8 @@ size_t sample_draw_smem(int top_k) {
 size_t select_sample_smem(int V) {
     int P = 1;
     while (P < V) P <<= 1;
-    return static_cast<size_t>(P) * (sizeof(uint64_t) + sizeof(int));
+    // keys (with one gap per 16 on the radix path), then the token order
+    return static_cast<size_t>(P + P / 16) * sizeof(uint64_t) + static_cast<size_t>(P) * sizeof(int);
 }
 
 cudaError_t launch_select_sample(cudaStream_t s, const float* logits, int rows, int V, int W,
