@@ -588,6 +588,31 @@ __global__ __launch_bounds__(kSingleThreads, 1) void k_gemm_tc(
                 const int m = m0 + r, n = n0 + c;
                 if (m < M && n < N) out[static_cast<size_t>(m) * N + n] = tile[r * LD + c];
             }
+        } else if (vector_epilogue_ok<E, 16>(ea, bias, N, 1, nullptr)) {
+            // 16-column chunks of a row per thread through the vector epilogue (16-byte loads
+            // and stores); chunks that stick out of the matrix go element by element.
+            constexpr int kChunks = BN / 16;
+            for (int e = t; e < BM * kChunks; e += 128) {
+                const int r = e / kChunks, c = (e - r * kChunks) * 16;
+                const int m = m0 + r, n = n0 + c;
+                if (m >= M || n >= N) continue;
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    v[j] = tile[r * LD + c + j];
+                    if (bias && n + j < N) v[j] = __fadd_rn(v[j], bias[n + j]);
+                }
+                if (n + 16 <= N) {
+                    int row_map = 0, row_slot = 0;
+                    if constexpr (E == Epi::kQkv || E == Epi::kLogits) {
+                        row_map = ea.rowmap[m];
+                        if constexpr (E == Epi::kQkv) row_slot = ea.slot[m];
+                    }
+                    epilogue_row<E, 16>(ea, m, n, v, M, N, 0, nullptr, row_map, row_slot);
+                } else {
+                    for (int j = 0; j < 16 && n + j < N; ++j) epi_apply<E>(ea, m, n + j, v[j]);
+                }
+            }
         } else {
             for (int e = t; e < BM * BN; e += 128) {
                 const int r = e / BN, c = e - r * BN;
