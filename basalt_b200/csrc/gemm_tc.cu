@@ -868,6 +868,57 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, int splits, int 
     }
 }
 
+// k_splitk_reduce with 8 consecutive columns per thread through the vector epilogue: the split
+// sums in the same order (then the bias), 16-byte loads of the partials and 16-byte stores.
+// Grid: x over column blocks of 8 * blockDim.x, y over rows (one row per block).
+template <Epi E>
+__global__ __launch_bounds__(256) void k_splitk_reduce_vec(const float* __restrict__ part,
+                                                          int splits, int M, int N,
+                                                          const float* __restrict__ bias,
+                                                          EpiArgs ea) {
+    constexpr int CW = 8;
+    const size_t total = static_cast<size_t>(M) * N;
+    const int n = (blockIdx.x * blockDim.x + threadIdx.x) * CW;
+    const int m = blockIdx.y;
+    float b[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) b[j] = bias && n + j < N ? bias[n + j] : 0.0f;  // a weight
+    pdl_trigger();
+    pdl_wait();
+    if (n >= N) return;
+    const float* src = part + static_cast<size_t>(m) * N + n;
+    float v[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = 0.0f;
+    for (int z0 = 0; z0 < splits; z0 += 4) {
+        float4 t[4][2];
+#pragma unroll
+        for (int z = 0; z < 4; ++z) {
+            if (z0 + z < splits) {
+                t[z][0] = __ldcg(reinterpret_cast<const float4*>(src + (z0 + z) * total));
+                t[z][1] = __ldcg(reinterpret_cast<const float4*>(src + (z0 + z) * total + 4));
+            }
+        }
+#pragma unroll
+        for (int z = 0; z < 4; ++z) {
+            if (z0 + z < splits) {
+                v[0] += t[z][0].x; v[1] += t[z][0].y; v[2] += t[z][0].z; v[3] += t[z][0].w;
+                v[4] += t[z][1].x; v[5] += t[z][1].y; v[6] += t[z][1].z; v[7] += t[z][1].w;
+            }
+        }
+    }
+    if (bias) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) v[j] = __fadd_rn(v[j], b[j]);
+    }
+    int row_map = 0, row_slot = 0;
+    if constexpr (E == Epi::kQkv || E == Epi::kLogits) {
+        row_map = ea.rowmap[m];
+        if constexpr (E == Epi::kQkv) row_slot = ea.slot[m];
+    }
+    epilogue_row<E, CW>(ea, m, n, v, M, N, 0, nullptr, row_map, row_slot);
+}
+
 // The split-K fix-up of the head when it folds the argmax: one block per row, so the row's
 // packed first maximum is reduced inside the block and stored with one plain write (no atomics).
 // The sums and the logits it writes are those of k_splitk_reduce<kLogits>.
@@ -1078,6 +1129,17 @@ struct SplitK {
     int tma = 0;         // the one-tile kernel stores the partials with the TMA unit
 };
 
+// Host-side counterpart of vector_epilogue_ok for the kStore / kGelu epilogues of an 8-column
+// vector fix-up: 16-byte aligned destinations whose row strides keep them so.
+bool host_vector_epilogue_ok(const EpiArgs& ea, int N) {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (ea.out && (!a16(ea.out) || ea.ldo % 4 != 0)) return false;
+    if (ea.split.planes) {
+        if (!a16(ea.split.hi) || !a16(ea.split.lo) || ea.split.ld % 8 != 0) return false;
+    }
+    return N % 8 == 0;
+}
+
 template <int FMT, int BN, Epi E>
 cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1,
                          const CUtensorMap& b0, const CUtensorMap& b1, const float* bias, int M,
@@ -1107,6 +1169,17 @@ cudaError_t launch_typed(cudaStream_t s, const CUtensorMap& a0, const CUtensorMa
         if (ea.best) {
             return launch_pdl(k_splitk_reduce_logits_best, dim3(M), dim3(256), 0, s, sk.part,
                               sk.splits, M, N, bias, ea);
+        }
+    }
+    if constexpr (E == Epi::kGelu || E == Epi::kStore) {
+        // Whole 8-column chunks, 16-byte aligned partials, bias and destinations: the vector
+        // fix-up (the split-K FFN1 of a decode lane).
+        const bool aligned = (reinterpret_cast<uintptr_t>(sk.part) & 15) == 0 &&
+                             (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
+        if (N % 8 == 0 && aligned && M <= 65535 && host_vector_epilogue_ok(ea, N)) {
+            const dim3 vgrid((N / 8 + 255) / 256, M);
+            return launch_pdl(k_splitk_reduce_vec<E>, vgrid, dim3(256), 0, s, sk.part, sk.splits,
+                              M, N, bias, ea);
         }
     }
     const dim3 rgrid((N + 255) / 256, std::min(M, std::max(1, 148 * 8 / ((N + 255) / 256))));
